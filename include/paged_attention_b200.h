@@ -1,0 +1,176 @@
+/*
+ * paged_attention_b200.h — C ABI of the B200 (sm_100a) paged-attention hot path.
+ *
+ * Drop-in for the attention seam of akshajravi/llm-inference-server:
+ *   inference_server/core/attention.py:73-88     paged_attention(query, k_pool, v_pool,
+ *                                                block_tables, context_lens, query_lens, scale)
+ *   inference_server/core/paged_executor.py:116-125  _PagedCache.update (KV append)
+ *   inference_server/core/paged_executor.py:211-263  _pack (per-step ragged metadata)
+ *
+ * Plain C types only: device pointers, element strides, sizes and a dtype enum.  The
+ * library owns no device memory: the caller allocates outputs, the packed metadata
+ * buffer and the workspace.  Every launch is asynchronous on the caller's stream and
+ * the entry points never synchronise the device.
+ *
+ * Pools use the reference layout bit for bit (inference_server/core/kv_pool.py:120):
+ * one contiguous [num_blocks, block_size, num_kv_heads, head_dim] tensor per layer for
+ * K and one for V.  A flat slot is block * block_size + offset
+ * (inference_server/core/block_table.py:143-159).
+ *
+ * Return codes: PA_OK or one of PA_ERR_*; pa_last_error() gives the message of the
+ * calling thread's most recent failure.  Contract violations use the reference's own
+ * message texts (inference_server/core/attention.py:202-219).
+ */
+#ifndef PAGED_ATTENTION_B200_H
+#define PAGED_ATTENTION_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PA_OK 0
+#define PA_ERR_INVALID_ARGUMENT 1   /* contract violation; maps to ValueError */
+#define PA_ERR_UNSUPPORTED 2        /* shape/dtype this build does not run */
+#define PA_ERR_CUDA 3               /* a CUDA runtime/driver call failed */
+#define PA_ERR_BUFFER_TOO_SMALL 4   /* metadata buffer or workspace too small */
+
+/* Storage dtype of query, pools and output (all three must match). */
+#define PA_DTYPE_F32 0
+#define PA_DTYPE_F16 1
+#define PA_DTYPE_BF16 2
+
+/*
+ * Per-step plan: sizes and the offsets (in int32 words) of every array inside the
+ * packed metadata buffer that pa_plan_step fills.  One plan serves every layer of a
+ * step, so the host builds and uploads metadata once per step, not once per layer.
+ */
+typedef struct pa_step_plan {
+  int32_t num_seqs;            /* B */
+  int32_t num_tokens;          /* T = sum(query_lens) */
+  int32_t table_width;         /* W: blocks per row of the packed int32 block table */
+  int32_t block_size;          /* tokens per pool block */
+  int32_t num_decode_seqs;     /* sequences with query_len == 1 */
+  int32_t num_prefill_seqs;    /* sequences with query_len > 1 */
+  int32_t num_prefill_tokens;  /* tokens of those sequences */
+  int32_t split_blocks;        /* pool blocks per decode split (split-K) */
+  int32_t num_decode_items;    /* decode work items = (sequence, split) pairs */
+  int32_t num_combine_seqs;    /* decode sequences with more than one split */
+  int32_t max_context;         /* max(context_lens) */
+  int32_t max_query_len;       /* max(query_lens) */
+  int32_t prefill_tile_tokens; /* query rows per prefill work tile (0: no tile list) */
+  int32_t num_prefill_tiles;   /* prefill work tiles = (sequence, first query row) */
+  int64_t total_context;       /* sum(context_lens) */
+  int64_t off_block_tables;    /* [B, W] physical block ids, 0-padded */
+  int64_t off_context_lens;    /* [B] tokens in the cache after this pass */
+  int64_t off_query_lens;      /* [B] new tokens per sequence */
+  int64_t off_cu_query_lens;   /* [B+1] exclusive prefix sum of query_lens */
+  int64_t off_seq_idx;         /* [T] sequence of each packed token */
+  int64_t off_q_pos;           /* [T] logical position ctx - q_len + t of each token */
+  int64_t off_slot_mapping;    /* [T] flat pool slot each new token's K/V is written to */
+  int64_t off_decode_items;    /* [num_decode_items][4] seq, split, part, nsplit */
+  int64_t off_combine;         /* [num_combine_seqs][4] seq, token, first part, nsplit */
+  int64_t off_prefill_tiles;   /* [num_prefill_tiles][2] seq, first query row */
+  int64_t words;               /* int32 words used in the packed buffer */
+} pa_step_plan;
+
+/* Version of this ABI (bumped on any signature or struct change). */
+int32_t pa_abi_version(void);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* pa_last_error(void);
+
+/*
+ * Upper bound on the int32 words pa_plan_step writes for a step with num_seqs
+ * sequences, num_tokens packed tokens and at most max_blocks_per_seq blocks per row.
+ */
+int64_t pa_plan_words_bound(int32_t num_seqs, int32_t num_tokens, int32_t max_blocks_per_seq);
+
+/*
+ * Validate one step's ragged batch and write its packed metadata into a HOST buffer
+ * (pinned memory makes the single upload asynchronous).  Replaces the per-layer
+ * validation of inference_server/core/attention.py:202-219 (_check), the per-token
+ * tables of inference_server/core/attention_triton.py:129-150 (_token_map) and the
+ * write-slot computation of inference_server/core/paged_executor.py:240-247.
+ *
+ *   context_lens, query_lens  host int64 [num_seqs]
+ *   block_tables              host int64, row i at block_tables + i * table_row_stride,
+ *                             table_cols entries per row (the reference's 0-padded rows)
+ *   num_tokens                the query's token count (must equal sum(query_lens))
+ *   pool_num_blocks           blocks in the pool; every block a sequence reads must be
+ *                             in [0, pool_num_blocks)
+ *   num_kv_heads, sm_count    used to size decode splits so the grid fills the GPU
+ *   prefill_tile_tokens       query rows per prefill tile (0 = no prefill tile list)
+ *   meta_out, meta_capacity   host int32 buffer and its size in words
+ *
+ * The upload of meta_out[0 .. plan->words) to a device buffer is the caller's (one
+ * cudaMemcpyAsync); the device copy is what pa_paged_attention_fwd and
+ * pa_reshape_and_cache read.
+ */
+int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int32_t num_seqs,
+                     const int64_t* block_tables, int64_t table_row_stride, int32_t table_cols,
+                     int32_t num_tokens, int64_t pool_num_blocks, int32_t block_size,
+                     int32_t num_kv_heads, int32_t sm_count, int32_t prefill_tile_tokens,
+                     int32_t* meta_out, int64_t meta_capacity, pa_step_plan* plan);
+
+/* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape. */
+uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim);
+
+/*
+ * Causal paged attention over a ragged batch: the computation of
+ * inference_server/core/attention.py:92-187 (paged_attention_gather), replacing the
+ * Triton kernel of inference_server/core/attention_triton.py:156-305.
+ *
+ *   query    [num_tokens, num_heads, head_dim], any element strides
+ *   k_pool   contiguous [pool_num_blocks, block_size, num_kv_heads, head_dim]
+ *   v_pool   same shape as k_pool
+ *   out      [num_tokens, num_heads, head_dim], strides out_stride_token/out_stride_head,
+ *            unit stride along head_dim
+ *   meta     device copy of the packed buffer pa_plan_step wrote for `plan`
+ *   workspace  at least pa_workspace_bytes(plan, num_heads, head_dim) device bytes,
+ *            256-byte aligned; it holds split-K partials and, in its first 4 bytes, a
+ *            device error word the caller zeroes once when it allocates the workspace
+ *   stream   cudaStream_t to launch on
+ *
+ * Token t of sequence i sits at position ctx_i - q_i + t and attends to keys 0..that.
+ * Scores, softmax and accumulation are float32; the output is stored in `dtype`.
+ */
+int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                               int64_t q_stride_dim, int32_t num_tokens, int32_t num_heads,
+                               int32_t head_dim, const void* k_pool, const void* v_pool,
+                               int64_t pool_num_blocks, int32_t block_size, int32_t num_kv_heads,
+                               int32_t dtype, float scale, const pa_step_plan* plan,
+                               const int32_t* meta, void* out, int64_t out_stride_token,
+                               int64_t out_stride_head, void* workspace, uint64_t workspace_bytes,
+                               void* stream);
+
+/*
+ * Fused K+V append: write the new tokens' keys and values into both pools at their
+ * flat slots.  Replaces the two index_copy_ calls of
+ * inference_server/core/paged_executor.py:116-125 (_PagedCache.update); the pool bytes
+ * after the call are identical to the reference's.
+ *
+ *   key, value     [num_tokens, num_kv_heads, head_dim] with the given element strides
+ *                  (unit stride along head_dim); same dtype as the pools
+ *   slot_mapping   device int32 [num_tokens], each in [0, pool_num_blocks * block_size)
+ */
+int32_t pa_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_stride_head,
+                             const void* value, int64_t v_stride_token, int64_t v_stride_head,
+                             int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t dtype, void* k_pool, void* v_pool, int64_t pool_num_blocks,
+                             int32_t block_size, const int32_t* slot_mapping, void* stream);
+
+/*
+ * Read (and clear, when clear != 0) the device error word a workspace carries.  It is
+ * set by kernels that met an out-of-range block id or slot (the host checks make this
+ * unreachable for planned steps) or a pipeline wait that ran out of its iteration
+ * limit.  Synchronises `stream`.  Returns PA_OK and stores the word in *error_word.
+ */
+int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_ATTENTION_B200_H */

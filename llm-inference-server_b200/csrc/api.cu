@@ -1,0 +1,285 @@
+// extern "C" entry points declared in include/paged_attention_b200.h: argument checks,
+// TMA descriptor encoding (cached per pool), workspace layout and kernel dispatch.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "kernels.h"
+#include "pa_common.cuh"
+#include "pa_host.h"
+
+namespace pa {
+
+// Workspace layout: [0, 256) device error word + padding, then split-K partials
+// (float2 (m, l) per part and head, then float[head_dim] per part and head).
+constexpr uint64_t kWsHeader = 256;
+
+static uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+static int elem_size(int dtype) { return dtype == PA_DTYPE_F32 ? 4 : 2; }
+
+static CUtensorMapDataType tma_dtype(int dtype) {
+  switch (dtype) {
+    case PA_DTYPE_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    case PA_DTYPE_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t base;
+  int64_t blocks;
+  int32_t bs, hkv, dim, dtype;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && blocks == o.blocks && bs == o.bs && hkv == o.hkv && dim == o.dim && dtype == o.dtype;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.base) ^ (std::hash<int64_t>()(k.blocks) * 31) ^ (size_t(k.dim) << 7) ^
+           (size_t(k.hkv) << 17) ^ size_t(k.dtype);
+  }
+};
+
+// The pool [NB, BS, Hkv, D] as a 3-D tensor (D, Hkv, NB*BS); box (D, 1, BS) is one
+// block of one KV head.  Descriptors are cached by pool address and shape: a serving
+// process has 2 pools per layer and encodes each once.
+static int32_t pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int hkv, int dim, int dtype,
+                               CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{reinterpret_cast<uintptr_t>(pool), num_blocks, bs, hkv, dim, dtype};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return PA_OK;
+    }
+  }
+  auto fn = encode_fn();
+  if (!fn) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  const int es = elem_size(dtype);
+  cuuint64_t gdim[3] = {cuuint64_t(dim), cuuint64_t(hkv), cuuint64_t(num_blocks) * cuuint64_t(bs)};
+  cuuint64_t gstride[2] = {cuuint64_t(dim) * es, cuuint64_t(hkv) * dim * es};
+  cuuint32_t box[3] = {cuuint32_t(dim), 1u, cuuint32_t(bs)};
+  cuuint32_t estride[3] = {1u, 1u, 1u};
+  CUtensorMap map;
+  CUresult r = fn(&map, tma_dtype(dtype), 3, const_cast<void*>(pool), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, map);
+  *out = map;
+  return PA_OK;
+}
+
+static int32_t cuda_fail(cudaError_t e, const char* what) {
+  return fail(PA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+}  // namespace pa
+
+extern "C" {
+
+uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim) {
+  if (!plan) return 0;
+  const uint64_t parts = uint64_t(plan->num_decode_items > 0 ? plan->num_decode_items : 0);
+  const uint64_t ml = pa::align_up(parts * num_heads * sizeof(float2), 256);
+  const uint64_t po = parts * num_heads * uint64_t(head_dim) * sizeof(float);
+  return pa::kWsHeader + ml + po;
+}
+
+int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                               int64_t q_stride_dim, int32_t num_tokens, int32_t num_heads,
+                               int32_t head_dim, const void* k_pool, const void* v_pool,
+                               int64_t pool_num_blocks, int32_t block_size, int32_t num_kv_heads,
+                               int32_t dtype, float scale, const pa_step_plan* plan,
+                               const int32_t* meta, void* out, int64_t out_stride_token,
+                               int64_t out_stride_head, void* workspace, uint64_t workspace_bytes,
+                               void* stream_ptr) {
+  using namespace pa;
+  if (!plan) return fail(PA_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_UNSUPPORTED, "dtype code %d is not float32, float16 or bfloat16", dtype);
+  if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "heads and head_dim must be positive");
+  if (num_heads % num_kv_heads)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%d query heads not divisible by %d kv heads", num_heads, num_kv_heads);
+  if (head_dim > 256) return fail(PA_ERR_UNSUPPORTED, "head_dim %d > 256 is not supported", head_dim);
+  if (plan->num_tokens != num_tokens)
+    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for %d tokens, query has %d", plan->num_tokens, num_tokens);
+  if (plan->block_size != block_size)
+    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for block_size %d, pool has %d", plan->block_size,
+                block_size);
+  if (num_tokens == 0) return PA_OK;
+  if (!query || !k_pool || !v_pool || !out || !meta || !workspace)
+    return fail(PA_ERR_INVALID_ARGUMENT, "NULL device pointer");
+  const uint64_t need = pa_workspace_bytes(plan, num_heads, head_dim);
+  if (workspace_bytes < need)
+    return fail(PA_ERR_BUFFER_TOO_SMALL, "workspace holds %llu bytes, %llu needed",
+                (unsigned long long)workspace_bytes, (unsigned long long)need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(PA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int* err = static_cast<int*>(workspace);
+  const uint64_t parts = uint64_t(plan->num_decode_items);
+  float2* part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + kWsHeader);
+  float* part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeader +
+                                           align_up(parts * num_heads * sizeof(float2), 256));
+  const int group = num_heads / num_kv_heads;
+  const float qscale = scale * kLog2e;
+  const int32_t* tables = meta + plan->off_block_tables;
+
+  // Decode rows go to the split-K kernel when it has an instantiation for the shape and
+  // the pool/query layouts meet its alignment needs; every other row goes to the
+  // generic kernel.
+  const bool fast_decode = plan->num_decode_seqs > 0 && decode_supported(dtype, head_dim, group, block_size) &&
+                           q_stride_dim == 1 && reinterpret_cast<uintptr_t>(k_pool) % 16 == 0 &&
+                           reinterpret_cast<uintptr_t>(v_pool) % 16 == 0;
+  if (fast_decode) {
+    CUtensorMap tk, tv;
+    int32_t rc = pool_tensor_map(k_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, &tk);
+    if (rc != PA_OK) return rc;
+    rc = pool_tensor_map(v_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, &tv);
+    if (rc != PA_OK) return rc;
+    DecodeParams p{};
+    p.q = query;
+    p.q_st = q_stride_token;
+    p.q_sh = q_stride_head;
+    p.out = out;
+    p.o_st = out_stride_token;
+    p.o_sh = out_stride_head;
+    p.tables = tables;
+    p.width = plan->table_width;
+    p.ctx_lens = meta + plan->off_context_lens;
+    p.cu_q = meta + plan->off_cu_query_lens;
+    p.items = reinterpret_cast<const int4*>(meta + plan->off_decode_items);
+    p.num_items = plan->num_decode_items;
+    p.part_o = part_o;
+    p.part_ml = part_ml;
+    p.num_heads = num_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.split_blocks = plan->split_blocks;
+    p.pool_blocks = int32_t(pool_num_blocks);
+    p.qscale = qscale;
+    p.err = err;
+    cudaError_t e = launch_decode(dtype, head_dim, group, tk, tv, p, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "split-K decode launch");
+    if (plan->num_combine_seqs > 0) {
+      CombineParams c{};
+      c.out = out;
+      c.o_st = out_stride_token;
+      c.o_sh = out_stride_head;
+      c.combine = reinterpret_cast<const int4*>(meta + plan->off_combine);
+      c.num_combine = plan->num_combine_seqs;
+      c.part_o = part_o;
+      c.part_ml = part_ml;
+      c.num_heads = num_heads;
+      c.head_dim = head_dim;
+      e = launch_combine(dtype, c, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "split-K combine launch");
+    }
+  }
+  const bool rest = fast_decode ? plan->num_prefill_tokens > 0 : true;
+  if (rest) {
+    GenericParams g{};
+    g.q = query;
+    g.q_st = q_stride_token;
+    g.q_sh = q_stride_head;
+    g.q_sd = q_stride_dim;
+    g.out = out;
+    g.o_st = out_stride_token;
+    g.o_sh = out_stride_head;
+    g.k_pool = k_pool;
+    g.v_pool = v_pool;
+    g.block_size = block_size;
+    g.num_kv_heads = num_kv_heads;
+    g.head_dim = head_dim;
+    g.num_heads = num_heads;
+    g.tables = tables;
+    g.width = plan->table_width;
+    g.seq_idx = meta + plan->off_seq_idx;
+    g.q_pos = meta + plan->off_q_pos;
+    g.query_lens = meta + plan->off_query_lens;
+    g.num_tokens = num_tokens;
+    g.skip_decode = fast_decode ? 1 : 0;
+    g.pool_blocks = pool_num_blocks;
+    g.qscale = qscale;
+    g.err = err;
+    cudaError_t e = launch_generic(dtype, g, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "generic attention launch");
+  }
+  return PA_OK;
+}
+
+int32_t pa_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_stride_head,
+                             const void* value, int64_t v_stride_token, int64_t v_stride_head,
+                             int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t dtype, void* k_pool, void* v_pool, int64_t pool_num_blocks,
+                             int32_t block_size, const int32_t* slot_mapping, void* stream_ptr) {
+  using namespace pa;
+  if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_UNSUPPORTED, "dtype code %d is not float32, float16 or bfloat16", dtype);
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "bad append shape");
+  if (num_tokens == 0) return PA_OK;
+  if (!key || !value || !k_pool || !v_pool || !slot_mapping)
+    return fail(PA_ERR_INVALID_ARGUMENT, "NULL device pointer");
+  const int es = elem_size(dtype);
+  AppendParams p{};
+  p.key = static_cast<const uint8_t*>(key);
+  p.k_st = k_stride_token * es;
+  p.k_sh = k_stride_head * es;
+  p.value = static_cast<const uint8_t*>(value);
+  p.v_st = v_stride_token * es;
+  p.v_sh = v_stride_head * es;
+  p.num_tokens = num_tokens;
+  p.num_kv_heads = num_kv_heads;
+  p.row_bytes = head_dim * es;
+  p.k_pool = static_cast<uint8_t*>(k_pool);
+  p.v_pool = static_cast<uint8_t*>(v_pool);
+  p.num_slots = pool_num_blocks * block_size;
+  p.slots = slot_mapping;
+  cudaError_t e = launch_append(p, static_cast<cudaStream_t>(stream_ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache launch");
+  return PA_OK;
+}
+
+int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream_ptr) {
+  using namespace pa;
+  if (!workspace || !error_word) return fail(PA_ERR_INVALID_ARGUMENT, "NULL pointer");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int32_t word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, workspace, sizeof(word), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (clear) {
+    e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  *error_word = word;
+  return PA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,88 @@
+// Host-side launchers of the device kernels (internal to the library).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pa {
+
+// Split-K decode over (sequence, split) work items, one CTA per item and KV head.
+struct DecodeParams {
+  const void* q;
+  int64_t q_st, q_sh;         // element strides of query (unit stride along head_dim)
+  void* out;
+  int64_t o_st, o_sh;         // element strides of out (unit stride along head_dim)
+  const int32_t* tables;      // [B, width]
+  int32_t width;
+  const int32_t* ctx_lens;    // [B]
+  const int32_t* cu_q;        // [B+1]
+  const int4* items;          // [num_items] seq, split, part, nsplit
+  int32_t num_items;
+  float* part_o;              // [parts, Hq, D]
+  float2* part_ml;            // [parts, Hq]: running max (log2 domain) and denominator
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t split_blocks;
+  int32_t pool_blocks;
+  float qscale;               // softmax scale * log2(e)
+  int* err;
+};
+
+struct CombineParams {
+  void* out;
+  int64_t o_st, o_sh;
+  const int4* combine;        // [num_combine] seq, token, first part, nsplit
+  int32_t num_combine;
+  const float* part_o;
+  const float2* part_ml;
+  int32_t num_heads;
+  int32_t head_dim;
+};
+
+// Generic kernel: any block size, head_dim <= 256, any strides; one warp per
+// (token, head).  Serves shapes outside the fast paths and prefill rows.
+struct GenericParams {
+  const void* q;
+  int64_t q_st, q_sh, q_sd;
+  void* out;
+  int64_t o_st, o_sh;
+  const void* k_pool;
+  const void* v_pool;
+  int32_t block_size, num_kv_heads, head_dim, num_heads;
+  const int32_t* tables;
+  int32_t width;
+  const int32_t* seq_idx;
+  const int32_t* q_pos;
+  const int32_t* query_lens;
+  int32_t num_tokens;
+  int32_t skip_decode;        // 1: tokens of query_len == 1 sequences are done elsewhere
+  int64_t pool_blocks;
+  float qscale;
+  int* err;
+};
+
+struct AppendParams {
+  const uint8_t* key;
+  int64_t k_st, k_sh;         // byte strides
+  const uint8_t* value;
+  int64_t v_st, v_sh;
+  int32_t num_tokens, num_kv_heads;
+  int32_t row_bytes;          // head_dim * element size
+  uint8_t* k_pool;
+  uint8_t* v_pool;
+  int64_t num_slots;
+  const int32_t* slots;
+};
+
+// Returns true when the fast decode kernel has an instantiation for this shape.
+bool decode_supported(int dtype, int head_dim, int group, int block_size);
+// Dynamic shared memory bytes of the decode kernel.
+int decode_smem_bytes(int dtype, int head_dim, int group);
+cudaError_t launch_decode(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
+                          const DecodeParams& p, cudaStream_t stream);
+cudaError_t launch_combine(int dtype, const CombineParams& p, cudaStream_t stream);
+cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream);
+cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
+
+}  // namespace pa

@@ -1,0 +1,163 @@
+"""Parity of the sm_100a attention path with the reference (golden vectors) and the CPU
+oracle, through the C ABI (ctypes) on a real GPU.
+
+Tolerances: fp32 atol = rtol = 1e-5 (the north star's 1e-5 relative; the reference's
+own kernel tier allows 1e-4, tests/test_paged_attention_triton.py:165-169), fp16/bf16
+2e-2 (tests/test_paged_attention_triton.py:172-178).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _batches import compact_subbatch, lognormal_contexts, ragged_batch, ragged_batch_device, subset_rows
+from _golden import TOL, attention_cases, load_attention
+
+pytestmark = pytest.mark.gpu
+
+DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+NAME = {v: k for k, v in DT.items()}
+DEV = "cuda"
+
+
+def _close(got: np.ndarray, ref: np.ndarray, dt: str, what: str = ""):
+    np.testing.assert_allclose(got, ref, err_msg=what, **TOL[dt])
+
+
+def _run(pkg, q, kp, vp, bt, cl, ql, scale):
+    out = pkg.paged_attention_cuda(q.to(DEV), kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), scale)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("case", attention_cases())
+def test_matches_reference_golden(pkg, case):
+    """Every shape the reference's test-suite uses plus the serving shapes, against the
+    reference gather path's own outputs."""
+    g = load_attention(case)
+    td = DT[g["dtype"]]
+    q = torch.from_numpy(g["query"]).to(td)
+    kp = torch.from_numpy(g["k_pool"]).to(td)
+    vp = torch.from_numpy(g["v_pool"]).to(td)
+    out = _run(pkg, q, kp, vp, torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]),
+               torch.from_numpy(g["query_lens"]), g["scale"])
+    assert out.dtype == td and tuple(out.shape) == g["out"].shape
+    _close(out.float().cpu().numpy(), g["out"], g["dtype"], case)
+    assert pkg.read_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("heads,kv_heads,d", [(12, 12, 64), (32, 8, 128), (64, 8, 128), (16, 8, 64), (8, 1, 128)])
+def test_split_k_decode_matches_oracle(pkg, oracle, dtype, heads, kv_heads, d):
+    """Long ragged decode batches: many splits per sequence, so the combine pass runs;
+    every GQA group the fast kernel instantiates (1, 2, 4, 8)."""
+    ctx = lognormal_contexts(24, 700, 0.9, 1, 3000, seed=heads + d)
+    lengths = [(int(c), 1) for c in ctx] + [(1, 1), (16, 1), (17, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=d, heads=heads, kv_heads=kv_heads, dtype=DT[dtype])
+    out = _run(pkg, q, kp, vp, bt, cl, ql, d ** -0.5)
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), d ** -0.5, dtype)
+    _close(out.float().cpu().numpy(), ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_mixed_prefill_and_decode(pkg, oracle, dtype):
+    """Decode rows on the split-K kernel and prefill / partial-query rows on the generic
+    kernel in one call (tests/test_paged_attention.py:123-135 shapes at block size 16)."""
+    lengths = [(300, 1), (16, 16), (129, 1), (64, 40), (90, 90), (33, 3), (1, 1), (700, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=32, kv_heads=8, dtype=DT[dtype], seed=5)
+    out = _run(pkg, q, kp, vp, bt, cl, ql, 128 ** -0.5)
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), 128 ** -0.5, dtype)
+    _close(out.float().cpu().numpy(), ref, dtype)
+
+
+def test_accepts_non_contiguous_query(pkg):
+    """The executor hands over `query[0].transpose(0, 1)` (tests/test_paged_attention_triton.py:209-220)."""
+    lengths = [(6, 1), (10, 10), (4, 1), (9, 5), (16, 16), (13, 1), (300, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=64, heads=12, kv_heads=12)
+    strided = q.to(DEV).transpose(0, 1).contiguous().transpose(0, 1)
+    assert not strided.is_contiguous()
+    a = pkg.paged_attention_cuda(strided, kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.125)
+    b = pkg.paged_attention_cuda(q.to(DEV), kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.125)
+    torch.testing.assert_close(a, b, atol=0, rtol=0)
+
+
+def test_fast_and_generic_kernels_agree(pkg):
+    """A query with non-unit dim stride routes decode rows to the generic kernel; both
+    kernels must give the same answer to fp32 rounding."""
+    lengths = [(int(c), 1) for c in lognormal_contexts(16, 400, 0.9, 1, 2000, seed=2)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=32, kv_heads=8)
+    q_dev = q.to(DEV)
+    odd = torch.empty(q.shape[0], q.shape[1], q.shape[2] * 2, device=DEV)[:, :, ::2]
+    odd.copy_(q_dev)
+    assert odd.stride(2) == 2
+    fast = pkg.paged_attention_cuda(q_dev, kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.088)
+    slow = pkg.paged_attention_cuda(odd, kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.088)
+    torch.testing.assert_close(fast, slow, atol=2e-6, rtol=2e-6)
+
+
+def test_empty_batch(pkg):
+    q = torch.empty(0, 3, 8, device=DEV)
+    pool = torch.zeros(4, 4, 3, 8, device=DEV)
+    zero = torch.zeros(0, dtype=torch.long, device=DEV)
+    out = pkg.paged_attention_cuda(q, pool, pool, torch.zeros(0, 1, dtype=torch.long, device=DEV), zero, zero, 0.5)
+    assert out.shape == (0, 3, 8)
+
+
+def test_contract_errors_on_device(pkg):
+    q, kp, vp, bt, cl, ql = ragged_batch([(4, 4), (2, 2)], bs=4, d=8, heads=3, kv_heads=3)
+    args = [t.to(DEV) for t in (q, kp, vp, bt)]
+    with pytest.raises(ValueError, match="query_len exceeds context_len"):
+        pkg.paged_attention_cuda(*args, (cl - 1).to(DEV), ql.to(DEV), 0.5)
+    with pytest.raises(ValueError, match="query_lens sum"):
+        pkg.paged_attention_cuda(args[0][:-1], *args[1:], cl.to(DEV), ql.to(DEV), 0.5)
+
+
+def test_deterministic_and_batch_order_invariant(pkg):
+    """Same inputs -> bitwise-equal outputs; permuting the sequences of a batch permutes
+    the outputs bitwise (each sequence's splits depend only on its own length and the
+    batch's length multiset)."""
+    lengths = [(int(c), 1) for c in lognormal_contexts(64, 1024, 0.9, 16, 8192, seed=9)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=64, heads=12, kv_heads=12, dtype=torch.bfloat16)
+    a = _run(pkg, q, kp, vp, bt, cl, ql, 0.125)
+    b = _run(pkg, q, kp, vp, bt, cl, ql, 0.125)
+    assert torch.equal(a, b)
+    perm = torch.randperm(len(lengths), generator=torch.Generator().manual_seed(1))
+    c = _run(pkg, q[perm], kp, vp, bt[perm], cl[perm], ql[perm], 0.125)
+    assert torch.equal(c, a[perm.to(DEV)])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_full_size_microbench_config_sampled(pkg, oracle, dtype):
+    """BASELINE config 2 at full size (B=256, GPT-2 heads, lognormal median 1024 clipped
+    16..8192): the whole batch runs on the GPU; 8 sampled sequences plus the longest are
+    re-computed by the oracle (a sequence's output depends only on its own blocks)."""
+    ctx = lognormal_contexts(256, 1024, 0.9, 16, 8192, seed=0)
+    lengths = [(int(c), 1) for c in ctx]
+    batch = ragged_batch_device(lengths, bs=16, d=64, heads=12, kv_heads=12, dtype=DT[dtype], device=DEV)
+    q, kp, vp, bt, cl, ql = batch
+    out = pkg.paged_attention_cuda(q, kp, vp, bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.125).float().cpu().numpy()
+    picks = list(np.random.default_rng(1).choice(256, size=8, replace=False)) + [int(np.argmax(ctx))]
+    sub = compact_subbatch(*batch, lengths, picks, 16)
+    ref = oracle.paged_attention_gather(*sub, 0.125, dtype)
+    _close(out[subset_rows(lengths, picks)], ref, dtype)
+
+
+def test_full_size_llama8b_decode_sampled(pkg, oracle):
+    """BASELINE config 3 decode shape at full size (B=256, 32/8/128 bf16, contexts
+    lognormal mean 4096 clipped 128..16384): one layer on the GPU, 4 sequences re-computed
+    by the oracle."""
+    ctx = lognormal_contexts(256, 4096 * np.exp(-0.405), 0.9, 128, 16384, seed=0)
+    lengths = [(int(c), 1) for c in ctx]
+    batch = ragged_batch_device(lengths, bs=16, d=128, heads=32, kv_heads=8, dtype=torch.bfloat16, device=DEV)
+    q, kp, vp, bt, cl, ql = batch
+    out = pkg.paged_attention_cuda(q, kp, vp, bt.to(DEV), cl.to(DEV), ql.to(DEV), 128 ** -0.5)
+    out = out.float().cpu().numpy()
+    picks = [int(np.argmax(ctx)), int(np.argmin(ctx)), 7, 100]
+    sub = compact_subbatch(*batch, lengths, picks, 16)
+    ref = oracle.paged_attention_gather(*sub, 128 ** -0.5, "bf16")
+    _close(out[subset_rows(lengths, picks)], ref, "bf16")
+    assert pkg.read_device_error() == 0

@@ -1,0 +1,181 @@
+"""Host-side logic and the C ABI, no GPU: the library loads and exports every symbol the
+public header declares; the C++ step planner reproduces the reference's integer
+metadata and contract errors; the seam keeps the gather path's signature and fails
+loudly off-GPU."""
+
+from __future__ import annotations
+
+import inspect
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from _golden import load
+
+REFERENCE_SIGNATURE = ["query", "k_pool", "v_pool", "block_tables", "context_lens", "query_lens", "scale"]
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.lib()
+    declared = pkg._lib.declared_symbols()
+    assert len(declared) == 8
+    for name in declared:
+        assert hasattr(lib, name), name
+    dyn = subprocess.run(["nm", "-D", "--defined-only", str(pkg._lib.LIB_PATH)], capture_output=True,
+                         text=True).stdout
+    for name in declared:
+        assert f" T {name}" in dyn, f"{name} is not a dynamic export"
+
+
+def test_abi_version_and_struct_size(pkg):
+    lib = pkg._lib.lib()
+    assert lib.pa_abi_version() == pkg._lib.ABI_VERSION
+    assert pkg._lib.ctypes.sizeof(pkg._lib.StepPlan) == 14 * 4 + 12 * 8
+
+
+def _plan(pkg, ctx, ql, tables, num_blocks=64, bs=4, kv_heads=1, sm=148, tile=0):
+    return pkg.StepMetadata.plan_host(ctx, ql, np.asarray(tables), num_tokens=int(np.sum(ql)),
+                                      pool_num_blocks=num_blocks, block_size=bs, num_kv_heads=kv_heads, sm=sm,
+                                      prefill_tile_tokens=tile)
+
+
+@pytest.mark.parametrize("tag", ["known", "random"])
+def test_planner_token_map_matches_reference(pkg, tag):
+    """seq_idx / q_pos / cu_query_lens of attention_triton.py:129-150, from the golden."""
+    z = load("token_map")
+    ctx, ql = z[f"{tag}_context_lens"], z[f"{tag}_query_lens"]
+    bs = 16
+    width = int(max(-(-c // bs) for c in ctx))
+    tables = np.zeros((len(ctx), width), dtype=np.int64)
+    m = _plan(pkg, ctx, ql, tables, num_blocks=1, bs=bs)
+    np.testing.assert_array_equal(m.seq_idx(False), z[f"{tag}_seq_idx"])
+    np.testing.assert_array_equal(m.q_pos(False), z[f"{tag}_q_pos"])
+    np.testing.assert_array_equal(m.cu_query_lens(False), z[f"{tag}_cu"])
+
+
+def test_planner_pack_matches_reference(pkg):
+    """write_slots, 0-padded block tables and lengths of the reference's _pack."""
+    z = load("pack")
+    m = _plan(pkg, z["context_lens"], z["query_lens"], z["block_tables"], num_blocks=64, bs=int(z["block_size"]))
+    np.testing.assert_array_equal(m.slot_mapping(False), z["write_slots"])
+    w = m.plan.table_width
+    np.testing.assert_array_equal(m.block_tables(False), z["block_tables"][:, :w])
+    assert m.plan.num_tokens == int(z["ends"][-1])
+
+
+def test_planner_matches_oracle_on_random_batches(pkg, oracle):
+    rng = np.random.default_rng(3)
+    for _ in range(20):
+        b = int(rng.integers(1, 40))
+        bs = int(rng.choice([4, 6, 16]))
+        ctx = rng.integers(1, 400, size=b)
+        ql = np.where(rng.random(b) < 0.6, 1, np.minimum(ctx, rng.integers(1, 60, size=b)))
+        need = -(-ctx // bs)
+        nb = int(need.sum()) + 5
+        perm = rng.permutation(nb)
+        width = int(need.max()) + int(rng.integers(0, 3))
+        tables = np.zeros((b, width), dtype=np.int64)
+        off = 0
+        for i in range(b):
+            tables[i, :need[i]] = perm[off:off + need[i]]
+            off += need[i]
+        m = _plan(pkg, ctx, ql, tables, num_blocks=nb, bs=bs, kv_heads=int(rng.choice([1, 8])),
+                  sm=int(rng.choice([8, 148])))
+        seqs = [(tables[i, :need[i]].tolist(), int(ctx[i] - ql[i]), int(ql[i])) for i in range(b)]
+        ref = oracle.pack_step(seqs, bs)
+        np.testing.assert_array_equal(m.slot_mapping(False), ref["write_slots"])
+        s, p, cu = oracle.token_map(ctx, ql)
+        np.testing.assert_array_equal(m.seq_idx(False), s)
+        np.testing.assert_array_equal(m.q_pos(False), p)
+        # split-K work list covers every decode block exactly once
+        items = m.decode_items()
+        sb = m.plan.split_blocks
+        covered = {}
+        for seq, split, part, ns in items.tolist():
+            assert ql[seq] == 1 and ns == -(-need[seq] // sb)
+            for blk in range(split * sb, min((split + 1) * sb, need[seq])):
+                covered[(seq, blk)] = covered.get((seq, blk), 0) + 1
+        expect = {(i, k) for i in range(b) if ql[i] == 1 for k in range(need[i])}
+        assert set(covered) == expect and all(v == 1 for v in covered.values())
+        parts = sorted(int(x) for x in items[:, 2])
+        assert parts == list(range(len(parts)))
+
+
+def test_planner_contract_errors_use_reference_messages(pkg):
+    t = np.zeros((2, 4), dtype=np.int64)
+    with pytest.raises(ValueError, match="query_lens sum"):
+        pkg.StepMetadata.plan_host([4, 2], [4, 2], t, num_tokens=5, pool_num_blocks=8, block_size=4,
+                                   num_kv_heads=1)
+    with pytest.raises(ValueError, match="query_len exceeds context_len"):
+        _plan(pkg, [3, 2], [4, 2], t)
+    with pytest.raises(ValueError, match="needs more blocks than its block_tables row holds"):
+        _plan(pkg, [17, 2], [1, 2], t)
+    with pytest.raises(ValueError, match="outside the pool"):
+        _plan(pkg, [5, 2], [1, 2], np.array([[3, 9], [1, 0]]), num_blocks=8)
+    with pytest.raises(ValueError, match="must be \\[batch\\]"):
+        _plan(pkg, [5, 2, 1], [1, 2, 1], t)
+
+
+def test_planner_empty_batch(pkg):
+    m = _plan(pkg, np.zeros(0, np.int64), np.zeros(0, np.int64), np.zeros((0, 1), np.int64))
+    assert m.plan.num_tokens == 0 and m.plan.num_decode_items == 0
+
+
+def test_split_size_fills_the_gpu(pkg):
+    """At the batch-256 / 4k-context decode shape the split keeps >= 8 CTAs per SM."""
+    rng = np.random.default_rng(0)
+    ctx = np.clip(np.exp(rng.normal(np.log(4096) - 0.405, 0.9, size=256)), 128, 16384).astype(np.int64)
+    need = -(-ctx // 16)
+    tables = np.zeros((256, int(need.max())), dtype=np.int64)
+    m = _plan(pkg, ctx, np.ones(256, np.int64), tables, num_blocks=1, bs=16, kv_heads=8)
+    assert m.plan.num_decode_items * 8 >= 148 * 8
+    assert 1 <= m.plan.split_blocks <= 32
+
+
+def test_seam_keeps_the_gather_signature(pkg, oracle):
+    """The reference pins the dispatcher and every backend to one parameter list
+    (tests/test_paged_attention.py:197-204); the cuda backend keeps it."""
+    for fn in (pkg.paged_attention_cuda, pkg.paged_attention):
+        assert list(inspect.signature(fn).parameters) == REFERENCE_SIGNATURE
+    assert list(inspect.signature(oracle.paged_attention_gather).parameters)[:7] == REFERENCE_SIGNATURE
+
+
+def test_cuda_path_fails_loudly_off_gpu(pkg, monkeypatch):
+    """No silent fallback (attention_triton.py:250-264): CPU tensors raise."""
+    q = torch.randn(5, 3, 8)
+    pool = torch.randn(8, 4, 3, 8)
+    bt = torch.tensor([[0, 1]])
+    ctx, ql = torch.tensor([5]), torch.tensor([5])
+    with pytest.raises(NotImplementedError, match="ATTENTION=cuda"):
+        pkg.paged_attention_cuda(q, pool, pool, bt, ctx, ql, 0.5)
+    monkeypatch.setenv("ATTENTION", "cuda")
+    with pytest.raises(NotImplementedError, match="CUDA device"):
+        pkg.paged_attention(q, pool, pool, bt, ctx, ql, 0.5)
+    monkeypatch.setenv("ATTENTION", "cuda-graphs")
+    with pytest.raises(ValueError, match="ATTENTION"):
+        pkg.paged_attention(q, pool, pool, bt, ctx, ql, 0.5)
+    with pytest.raises(NotImplementedError, match="CUDA device"):
+        pkg.reshape_and_cache(q[:, :3], q[:, :3], pool, pool, torch.zeros(5, dtype=torch.int32))
+
+
+def test_shape_errors_match_reference(pkg):
+    pool = torch.randn(8, 4, 3, 8)
+    with pytest.raises(ValueError, match="query must be"):
+        pkg.paged_attention_cuda(torch.randn(5, 8), pool, pool, None, None, None, 0.5)
+    with pytest.raises(ValueError, match="k_pool must be"):
+        pkg.paged_attention_cuda(torch.randn(5, 3, 8), pool[0], pool[0], None, None, None, 0.5)
+
+
+def test_words_bound_covers_plans(pkg):
+    lib = pkg._lib.lib()
+    rng = np.random.default_rng(1)
+    for _ in range(10):
+        b = int(rng.integers(1, 64))
+        ctx = rng.integers(1, 3000, size=b)
+        ql = np.where(rng.random(b) < 0.5, 1, np.minimum(ctx, 50))
+        need = -(-ctx // 16)
+        tables = np.zeros((b, int(need.max())), dtype=np.int64)
+        m = _plan(pkg, ctx, ql, tables, num_blocks=1, bs=16, kv_heads=8, sm=148, tile=64)
+        assert m.plan.words <= lib.pa_plan_words_bound(b, int(ql.sum()), int(need.max()))

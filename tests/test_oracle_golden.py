@@ -1,0 +1,97 @@
+"""The CPU oracle against the reference's own outputs (committed golden vectors).
+
+These pin the oracle before anything is compared with it: every attention case the
+generator recorded from the reference's ``paged_attention_gather``, the reference
+test-suite's known-answer ``_token_map`` case, ``_pack`` over real reference sequences
+and the pool after ``_PagedCache.update``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _golden import attention_cases, load, load_attention
+
+CASES = attention_cases()
+
+
+def test_golden_set_is_complete():
+    # 9 reference test shapes + 2 more padding seeds + GQA + non-pow2 + 2 half dtypes
+    # + 7 block-size-16 serving shapes.
+    assert len(CASES) == 22
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_matches_reference_gather(case, oracle):
+    g = load_attention(case)
+    out = oracle.paged_attention_gather(g["query"], g["k_pool"], g["v_pool"], g["block_tables"],
+                                        g["context_lens"], g["query_lens"], g["scale"], g["dtype"])
+    assert out.shape == g["out"].shape
+    if g["dtype"] == "f32":
+        np.testing.assert_allclose(out, g["out"], atol=2e-6, rtol=2e-6)
+    else:
+        # Same rounding points as torch; residual differences come from the float32
+        # accumulation order inside the two matmuls, then one half-precision rounding.
+        ulp = 2.0 ** -7 if g["dtype"] == "bf16" else 2.0 ** -10
+        np.testing.assert_allclose(out, g["out"], atol=2 * ulp, rtol=2 * ulp)
+
+
+def test_token_map_known_answer(oracle):
+    """tests/test_paged_attention_triton.py:140-147 of the reference."""
+    s, p, cu = oracle.token_map([6, 10, 4], [1, 3, 4])
+    assert s.tolist() == [0, 1, 1, 1, 2, 2, 2, 2]
+    assert p.tolist() == [5, 7, 8, 9, 0, 1, 2, 3]
+    assert cu.tolist() == [0, 1, 4, 8]
+
+
+@pytest.mark.parametrize("tag", ["known", "random"])
+def test_token_map_matches_reference(tag, oracle):
+    z = load("token_map")
+    s, p, cu = oracle.token_map(z[f"{tag}_context_lens"], z[f"{tag}_query_lens"])
+    np.testing.assert_array_equal(s, z[f"{tag}_seq_idx"])
+    np.testing.assert_array_equal(p, z[f"{tag}_q_pos"])
+    np.testing.assert_array_equal(cu, z[f"{tag}_cu"])
+
+
+def test_pack_matches_reference(oracle):
+    z = load("pack")
+    seqs = [(z["blocks"][i][: z["num_blocks_per_seq"][i]].tolist(), int(z["num_cached"][i]),
+             int(z["num_new"][i])) for i in range(len(z["num_cached"]))]
+    got = oracle.pack_step(seqs, int(z["block_size"]))
+    for key in ("write_slots", "block_tables", "context_lens", "query_lens", "ends", "position_ids"):
+        np.testing.assert_array_equal(got[key], z[key], err_msg=key)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_kv_append_matches_reference(dt, oracle):
+    z = load(f"kv_append_{dt}")
+    # [1, H, T, D] -> [T, H, D], the layout _PagedCache.update scatters.
+    key = z["key"][0].transpose(1, 0, 2)
+    val = z["value"][0].transpose(1, 0, 2)
+    np.testing.assert_array_equal(oracle.kv_append(z["k_before"], z["write_slots"], key), z["k_after"])
+    np.testing.assert_array_equal(oracle.kv_append(z["v_before"], z["write_slots"], val), z["v_after"])
+
+
+def test_slots_raise_past_capacity(oracle):
+    with pytest.raises(IndexError):
+        oracle.slots([3, 1], 16, 33)
+    assert oracle.slots([3, 1], 16, 18).tolist() == list(range(48, 64)) + [16, 17]
+
+
+def test_oracle_contract_errors(oracle):
+    """Same ValueError texts as the reference's _check (tests/test_paged_attention.py:165-179)."""
+    g = load_attention("prefill_on_boundary")
+    args = (g["query"], g["k_pool"], g["v_pool"], g["block_tables"])
+    with pytest.raises(ValueError, match="query_len exceeds context_len"):
+        oracle.paged_attention_gather(*args, g["context_lens"] - 1, g["query_lens"], g["scale"])
+    with pytest.raises(ValueError, match="query_lens sum"):
+        oracle.paged_attention_gather(g["query"][:-1], *args[1:], g["context_lens"], g["query_lens"], g["scale"])
+
+
+def test_bf16_rounding_is_nearest_even(oracle):
+    x = np.array([1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8, -2.5, np.inf, 1e-40], dtype=np.float32)
+    r = oracle.round_to(x, "bf16")
+    assert r[0] == 1.0                      # tie -> even
+    assert r[1] == 1.0 + 2.0 ** -6          # tie -> even (up)
+    assert r[2] == -2.5 and np.isinf(r[3])
