@@ -53,6 +53,26 @@ FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
 
 
+def clipped_lognormal_mu(mean: float, sigma: float, lo: float, hi: float) -> float:
+    """mu such that E[clip(exp(N(mu, sigma)), lo, hi)] == mean (bisection on the closed
+    form), so "mean 4096 clipped to 128..16384" holds after the clip."""
+    from math import erf, exp, log, sqrt
+
+    def cdf(x):
+        return 0.5 * (1.0 + erf(x / sqrt(2.0)))
+
+    def clipped_mean(mu):
+        a, b = (log(lo) - mu) / sigma, (log(hi) - mu) / sigma
+        mid = exp(mu + sigma * sigma / 2) * (cdf(b - sigma) - cdf(a - sigma))
+        return lo * cdf(a) + mid + hi * (1.0 - cdf(b))
+
+    a, b = log(lo), log(hi)
+    for _ in range(100):
+        m = 0.5 * (a + b)
+        a, b = (m, b) if clipped_mean(m) < mean else (a, m)
+    return 0.5 * (a + b)
+
+
 class Workload:
     """The seeded decode batch of one rank."""
 
@@ -61,8 +81,7 @@ class Workload:
         self.batch, self.layers, self.heads, self.kv_heads = batch, layers, heads, kv_heads
         self.head_dim, self.block_size = head_dim, block_size
         rng = np.random.default_rng(seed)
-        # lognormal with mean `mean_ctx` before clipping: mu = ln(mean) - sigma^2/2
-        mu = np.log(mean_ctx) - sigma ** 2 / 2
+        mu = clipped_lognormal_mu(mean_ctx, sigma, lo, hi)
         self.ctx0 = np.clip(np.exp(rng.normal(mu, sigma, size=batch)), lo, hi).astype(np.int64)
         need = -(-(self.ctx0 + max_steps) // block_size)
         self.num_blocks = int(need.sum()) + 16
@@ -397,7 +416,8 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     bytes_per_call = float(np.mean([wl.attention_bytes(args.warmup + k, elem) for k in range(args.steps)]))
     achieved = bytes_per_call / (attn_avg_ms / 1e3) / 1e9
     peak, peak_kind = _measured_hbm()
-    traffic = _traffic_per_call(wl, elem)
+    traffic = _traffic_per_call(float(np.mean([wl.context_lens(args.warmup + k).sum()
+                                               for k in range(args.steps)])))
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -433,16 +453,17 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def _traffic_per_call(wl: Workload, elem: int):
-    """DRAM bytes per attention launch from the committed ncu summary, scaled from the
-    captured case to this workload by context tokens (traffic grows with them)."""
-    p = ROOT / "profiles" / "decode_traffic.json"
+def _traffic_per_call(ctx_tokens: float):
+    """DRAM bytes per decode launch from the committed ncu summary, scaled from the
+    captured case to this workload by context tokens (traffic grows with the K/V bytes
+    streamed, which are proportional to them)."""
+    p = ROOT / "profiles" / "paged_decode_splitk_traffic.txt"
     if not p.exists():
         return None
     try:
-        t = json.loads(p.read_text())
-        per_ctx_token = float(t["dram_bytes_per_launch"]) / float(t["context_tokens"])
-        return per_ctx_token * float(wl.ctx0.sum())
+        kv = dict(line.split("=", 1) for line in p.read_text().splitlines()
+                  if "=" in line and not line.startswith("#"))
+        return float(kv["dram_bytes_per_launch"]) / float(kv["context_tokens"]) * ctx_tokens
     except Exception:
         return None
 
