@@ -145,6 +145,30 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
                                int64_t out_stride_head, void* workspace, uint64_t workspace_bytes,
                                void* stream);
 
+/* Size of the static scratch pa_paged_attention_fwd_noalloc uses (32 MiB per GPU). */
+#define PA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * pa_paged_attention_fwd without a workspace argument, for callers that cannot
+ * allocate device memory (a plug-in inside a host framework that owns all device
+ * memory, a serving loop that cannot pay cudaMalloc's device-wide synchronisation).
+ * No counterpart in the reference: its gather path allocates freely through torch.
+ *
+ * The split-K scratch lives in a static device array of PA_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading this library reserves until the process exits; steps whose
+ * pa_workspace_bytes exceeds it are rejected with PA_ERR_BUFFER_TOO_SMALL.  The first
+ * call on a device looks the array's address up (make it before any stream capture).
+ * All calls share the array: the kernels' error word in it is cleared at the start of
+ * each call, and calls whose GPU work overlaps race on it.  Allocates nothing.
+ */
+int32_t pa_paged_attention_fwd_noalloc(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                                       int64_t q_stride_dim, int32_t num_tokens, int32_t num_heads,
+                                       int32_t head_dim, const void* k_pool, const void* v_pool,
+                                       int64_t pool_num_blocks, int32_t block_size, int32_t num_kv_heads,
+                                       int32_t dtype, float scale, const pa_step_plan* plan,
+                                       const int32_t* meta, void* out, int64_t out_stride_token,
+                                       int64_t out_stride_head, void* stream);
+
 /*
  * Fused K+V append: write the new tokens' keys and values into both pools at their
  * flat slots.  Replaces the two index_copy_ calls of

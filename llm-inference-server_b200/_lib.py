@@ -27,6 +27,8 @@ PA_DTYPE_F32 = 0
 PA_DTYPE_F16 = 1
 PA_DTYPE_BF16 = 2
 
+PA_NOALLOC_SCRATCH_BYTES = 32 << 20
+
 ABI_VERSION = 1
 
 
@@ -81,6 +83,10 @@ _SIGNATURES = {
                                        c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                                        c_void_p, c_void_p]),
     "pa_read_device_error": (c_int32, [c_void_p, c_int32, POINTER(c_int32), c_void_p]),
+    "pa_paged_attention_fwd_noalloc": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32,
+                                                 c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_float,
+                                                 POINTER(StepPlan), c_void_p, c_void_p, c_int64, c_int64,
+                                                 c_void_p]),
 }
 
 _lib = None
