@@ -46,26 +46,29 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 struct MapKey {
   uintptr_t base;
   int64_t blocks;
-  int32_t bs, hkv, dim, dtype;
+  int32_t bs, hkv, dim, dtype, box_inner, swizzle;
   bool operator==(const MapKey& o) const {
-    return base == o.base && blocks == o.blocks && bs == o.bs && hkv == o.hkv && dim == o.dim && dtype == o.dtype;
+    return base == o.base && blocks == o.blocks && bs == o.bs && hkv == o.hkv && dim == o.dim &&
+           dtype == o.dtype && box_inner == o.box_inner && swizzle == o.swizzle;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<uintptr_t>()(k.base) ^ (std::hash<int64_t>()(k.blocks) * 31) ^ (size_t(k.dim) << 7) ^
-           (size_t(k.hkv) << 17) ^ size_t(k.dtype);
+           (size_t(k.hkv) << 17) ^ size_t(k.dtype) ^ (size_t(k.box_inner) << 27) ^ (size_t(k.swizzle) << 40);
   }
 };
 
-// The pool [NB, BS, Hkv, D] as a 3-D tensor (D, Hkv, NB*BS); box (D, 1, BS) is one
-// block of one KV head.  Descriptors are cached by pool address and shape: a serving
-// process has 2 pools per layer and encodes each once.
+// The pool [NB, BS, Hkv, D] as a 3-D tensor (D, Hkv, NB*BS); box (box_inner, 1, BS) is
+// (part of) one block of one KV head: the whole row without swizzle for the SIMT kernel,
+// 64-element (128-byte) column halves with 128B swizzle for the tensor-pipe kernel.
+// Descriptors are cached by pool address and shape: a serving process has 2 pools per
+// layer and encodes each once.
 static int32_t pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int hkv, int dim, int dtype,
-                               CUtensorMap* out) {
+                               int box_inner, bool swizzle128, CUtensorMap* out) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  const MapKey key{reinterpret_cast<uintptr_t>(pool), num_blocks, bs, hkv, dim, dtype};
+  const MapKey key{reinterpret_cast<uintptr_t>(pool), num_blocks, bs, hkv, dim, dtype, box_inner, swizzle128 ? 1 : 0};
   {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
@@ -79,11 +82,12 @@ static int32_t pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int
   const int es = elem_size(dtype);
   cuuint64_t gdim[3] = {cuuint64_t(dim), cuuint64_t(hkv), cuuint64_t(num_blocks) * cuuint64_t(bs)};
   cuuint64_t gstride[2] = {cuuint64_t(dim) * es, cuuint64_t(hkv) * dim * es};
-  cuuint32_t box[3] = {cuuint32_t(dim), 1u, cuuint32_t(bs)};
+  cuuint32_t box[3] = {cuuint32_t(box_inner), 1u, cuuint32_t(bs)};
   cuuint32_t estride[3] = {1u, 1u, 1u};
   CUtensorMap map;
   CUresult r = fn(&map, tma_dtype(dtype), 3, const_cast<void*>(pool), gdim, gstride, box, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
   std::lock_guard<std::mutex> g(mu);
@@ -157,11 +161,17 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
   const bool fast_decode = plan->num_decode_seqs > 0 && decode_supported(dtype, head_dim, group, block_size) &&
                            q_stride_dim == 1 && reinterpret_cast<uintptr_t>(k_pool) % 16 == 0 &&
                            reinterpret_cast<uintptr_t>(v_pool) % 16 == 0;
+  // 16-bit pools take the tensor-pipe kernel when q rows can be read as 32-bit pairs.
+  const bool use_mma = fast_decode && decode_mma_supported(dtype, head_dim, group, block_size) &&
+                       q_stride_token % 2 == 0 && q_stride_head % 2 == 0 &&
+                       reinterpret_cast<uintptr_t>(query) % 4 == 0;
   if (fast_decode) {
     CUtensorMap tk, tv;
-    int32_t rc = pool_tensor_map(k_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, &tk);
+    const int box = use_mma ? 64 : head_dim;
+    int32_t rc = pool_tensor_map(k_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, box, use_mma,
+                                 &tk);
     if (rc != PA_OK) return rc;
-    rc = pool_tensor_map(v_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, &tv);
+    rc = pool_tensor_map(v_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, box, use_mma, &tv);
     if (rc != PA_OK) return rc;
     DecodeParams p{};
     p.q = query;
@@ -184,7 +194,8 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
     p.pool_blocks = int32_t(pool_num_blocks);
     p.qscale = qscale;
     p.err = err;
-    cudaError_t e = launch_decode(dtype, head_dim, group, tk, tv, p, stream);
+    cudaError_t e = use_mma ? launch_decode_mma(dtype, head_dim, group, tk, tv, p, stream)
+                            : launch_decode(dtype, head_dim, group, tk, tv, p, stream);
     if (e != cudaSuccess) return cuda_fail(e, "split-K decode launch");
     if (plan->num_combine_seqs > 0) {
       CombineParams c{};

@@ -82,6 +82,10 @@ int decode_smem_bytes(int dtype, int head_dim, int group);
 cudaError_t launch_decode(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
                           const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_combine(int dtype, const CombineParams& p, cudaStream_t stream);
+// Tensor-pipe decode (bf16/fp16): pools described with 64-element boxes and 128B swizzle.
+bool decode_mma_supported(int dtype, int head_dim, int group, int block_size);
+cudaError_t launch_decode_mma(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
+                              const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 

@@ -161,3 +161,27 @@ def test_full_size_llama8b_decode_sampled(pkg, oracle):
     ref = oracle.paged_attention_gather(*sub, 128 ** -0.5, "bf16")
     _close(out[subset_rows(lengths, picks)], ref, "bf16")
     assert pkg.read_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("heads,kv_heads,d", [(32, 8, 128), (64, 8, 128), (12, 12, 64), (16, 8, 64)])
+def test_tensor_pipe_and_simt_decode_agree(pkg, oracle, dtype, heads, kv_heads, d):
+    """16-bit decode rows run on the tensor-pipe kernel; a query whose head stride is odd
+    cannot be read as 32-bit pairs and routes the same rows to the SIMT decode kernel.
+    Both must match the oracle, and each other to the rounding of P to the pool dtype."""
+    ctx = lognormal_contexts(20, 600, 0.9, 1, 2500, seed=d + heads)
+    lengths = [(int(c), 1) for c in ctx] + [(15, 1), (16, 1), (17, 1), (31, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=d, heads=heads, kv_heads=kv_heads, dtype=DT[dtype],
+                                         seed=7)
+    qd = q.to(DEV)
+    odd = torch.empty(q.shape[0], q.shape[1], d + 1, dtype=qd.dtype, device=DEV)[:, :, :d]
+    odd.copy_(qd)
+    assert odd.stride(1) % 2 == 1 and odd.stride(2) == 1
+    args = (kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
+    mma = pkg.paged_attention_cuda(qd, *args).float().cpu().numpy()
+    simt = pkg.paged_attention_cuda(odd, *args).float().cpu().numpy()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), d ** -0.5, dtype)
+    _close(mma, ref, dtype, "tensor-pipe decode")
+    _close(simt, ref, dtype, "SIMT decode")
+    np.testing.assert_allclose(mma, simt, atol=1e-2, rtol=1e-2)
