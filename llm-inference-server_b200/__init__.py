@@ -9,6 +9,9 @@ The reference's attention seam with ``ATTENTION=cuda``:
 * ``StepMetadata`` — the step's ragged metadata planned once on the host and uploaded
   with a single copy (inference_server/core/paged_executor.py:211-263).
 
+``executor.CudaPagedExecutor`` is the reference's ``PagedExecutor`` on this path
+(imported on demand: it needs ``transformers``).
+
 The directory name is not a Python identifier; the package is imported under the name
 ``llm_inference_server_b200`` (see ``__graft_entry__.import_package``).
 """
@@ -16,7 +19,7 @@ The directory name is not a Python identifier; the package is imported under the
 from __future__ import annotations
 
 from .attention import paged_attention, paged_attention_cuda, read_device_error
-from .kv_cache import allocate_pool, reshape_and_cache
+from .kv_cache import KVPool, allocate_pool, reshape_and_cache
 from .metadata import StepMetadata, attach, attached
 
 __all__ = [
@@ -25,6 +28,7 @@ __all__ = [
     "read_device_error",
     "reshape_and_cache",
     "allocate_pool",
+    "KVPool",
     "StepMetadata",
     "attach",
     "attached",

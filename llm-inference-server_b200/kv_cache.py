@@ -56,3 +56,37 @@ def allocate_pool(num_layers: int, num_blocks: int, block_size: int, num_kv_head
     k = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
     v = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
     return k, v
+
+
+class KVPool:
+    """Per-layer K and V pools in the reference's layout with the attributes its executor
+    reads (inference_server/core/kv_pool.py:106-139): ``k``/``v`` lists of
+    ``[num_blocks, block_size, Hkv, D]`` zero-initialised tensors, ``num_blocks``,
+    ``block_size``."""
+
+    def __init__(self, num_layers: int, num_blocks: int, block_size: int, num_kv_heads: int, head_dim: int,
+                 dtype: torch.dtype, device) -> None:
+        self.num_blocks, self.block_size = num_blocks, block_size
+        self.num_kv_heads, self.head_dim, self.dtype = num_kv_heads, head_dim, dtype
+        self.k, self.v = allocate_pool(num_layers, num_blocks, block_size, num_kv_heads, head_dim, dtype, device)
+
+    @classmethod
+    def from_model(cls, model, num_blocks: int, block_size: int = 16, dtype=None, device=None) -> "KVPool":
+        """Sizes read off the model config the way ``ModelDims.from_model`` does
+        (kv_pool.py:47-61): ``num_key_value_heads`` when present, else full multi-head."""
+        cfg = model.config
+        heads = getattr(cfg, "num_attention_heads", None) or cfg.n_head
+        hidden = getattr(cfg, "hidden_size", None) or cfg.n_embd
+        layers = getattr(cfg, "num_hidden_layers", None) or cfg.n_layer
+        kv_heads = getattr(cfg, "num_key_value_heads", None) or heads
+        head_dim = getattr(cfg, "head_dim", None) or hidden // heads
+        p = next(model.parameters())
+        return cls(layers, num_blocks, block_size, kv_heads, head_dim, dtype or p.dtype, device or p.device)
+
+    @property
+    def num_slots(self) -> int:
+        return self.num_blocks * self.block_size
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.k + self.v)

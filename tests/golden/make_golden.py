@@ -18,6 +18,10 @@ What it records, all from the reference's own code on CPU:
   tables, context/query lengths, position ids.
 * ``kv_append_<dtype>.npz``: pool contents after ``_PagedCache.update``
   (paged_executor.py:116-125).
+* ``gpt2_greedy_cpu.npz``: greedy tokens of the reference's own ``PagedExecutor`` with
+  the gather path (paged_executor.py:162-295) on CPU, driving a random-init GPT-2 124M
+  (``GPT2LMHeadModel(GPT2Config())`` after ``torch.manual_seed(0)``, fp32) over three
+  prompts of random token ids for six steps (one prefill, five decodes).
 
 Half-precision tensors are stored as their raw 16-bit patterns (uint16 arrays; the
 ``dtype`` entry says which format), float32 tensors as float32, so every stored value
@@ -109,7 +113,10 @@ def _store(t: torch.Tensor, dtype: str) -> np.ndarray:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the llm-inference-server checkout")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="regenerate only these outputs: attn token_map pack kv_append gpt2_greedy")
     args = ap.parse_args()
+    want = set(args.only) if args.only else {"attn", "token_map", "pack", "kv_append", "gpt2_greedy"}
     os.environ.setdefault("DEVICE", "cpu")
     sys.path.insert(0, str(Path(args.reference).resolve()))
 
@@ -121,7 +128,7 @@ def main() -> None:
     from inference_server.core.paged_executor import PagedExecutor, _PagedCache, _StepContext
     from inference_server.core.sequence import Sequence
 
-    for name, (lengths, kw) in CASES.items():
+    for name, (lengths, kw) in (CASES.items() if "attn" in want else ()):
         q, kp, vp, bt, cl, ql = build(lengths, **kw)
         scale = kw["d"] ** -0.5
         out = paged_attention_gather(q, kp, vp, bt, cl, ql, scale)
@@ -132,6 +139,11 @@ def main() -> None:
             out=_store(out, dt), block_tables=bt.numpy(), context_lens=cl.numpy(),
             query_lens=ql.numpy(), scale=np.float64(scale), dtype=np.bytes_(dt),
         )
+
+    if "gpt2_greedy" in want:
+        _gpt2_greedy(PagedExecutor, PagedKVPool, ModelDims, BlockAllocator, BlockTable, Sequence)
+    if not want & {"token_map", "pack", "kv_append"}:
+        return
 
     # _token_map: the reference test's known answer plus a random ragged batch.
     rng = np.random.default_rng(7)
@@ -199,6 +211,32 @@ def main() -> None:
             k_after=_store(pool.k[1], dt), v_after=_store(pool.v[1], dt), dtype=np.bytes_(dt),
         )
     print(f"wrote {len(CASES)} attention cases + token_map, pack, kv_append to {HERE}")
+
+
+def _gpt2_greedy(PagedExecutor, PagedKVPool, ModelDims, BlockAllocator, BlockTable, Sequence) -> None:
+    """Greedy tokens of the reference executor on a seeded random-init GPT-2 (CPU)."""
+    from transformers import GPT2Config, GPT2LMHeadModel
+
+    torch.manual_seed(0)
+    model = GPT2LMHeadModel(GPT2Config()).eval()
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, 50257, size=int(rng.integers(16, 257))).tolist() for _ in range(3)]
+    nb, steps = 96, 6
+    pool = PagedKVPool(ModelDims(12, 12, 64, torch.float32), num_blocks=nb, block_size=16, device="cpu")
+    ex = PagedExecutor(model, None, pool)
+    alloc = BlockAllocator(nb)
+    seqs = [Sequence(seq_id=str(i), prompt_token_ids=p, max_tokens=100) for i, p in enumerate(prompts)]
+    for s in seqs:
+        s.block_table = BlockTable(alloc, 16)
+    for _ in range(steps):
+        for s in seqs:
+            s.block_table.ensure_capacity(s.num_cached + len(s.next_input_ids))
+        for s, tok in zip(seqs, ex.execute(seqs)):
+            s.output_token_ids.append(tok)
+    lens = np.array([len(p) for p in prompts])
+    np.savez_compressed(HERE / "gpt2_greedy_cpu.npz", prompt_lens=lens, prompts=np.concatenate(prompts),
+                        tokens=np.array([s.output_token_ids for s in seqs]), num_blocks=np.int64(nb),
+                        steps=np.int64(steps))
 
 
 if __name__ == "__main__":

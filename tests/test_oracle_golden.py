@@ -95,3 +95,21 @@ def test_bf16_rounding_is_nearest_even(oracle):
     assert r[0] == 1.0                      # tie -> even
     assert r[1] == 1.0 + 2.0 ** -6          # tie -> even (up)
     assert r[2] == -2.5 and np.isinf(r[3])
+
+
+def test_oracle_executor_reproduces_reference_greedy_tokens():
+    """The oracle executor (tests/_engine.py) that the GPU token-parity tests compare the
+    CUDA executor against reproduces the reference's own PagedExecutor token for token
+    (random-init GPT-2 124M, fp32, CPU; golden made by the reference)."""
+    import torch
+    from transformers import GPT2Config, GPT2LMHeadModel
+
+    from _engine import OracleExecutor, generate
+
+    z = load("gpt2_greedy_cpu")
+    prompts = [p.tolist() for p in np.split(z["prompts"], np.cumsum(z["prompt_lens"])[:-1])]
+    torch.manual_seed(0)
+    model = GPT2LMHeadModel(GPT2Config()).eval()
+    nb = int(z["num_blocks"])
+    tokens = generate(OracleExecutor(model, 12, nb, 16, 12, 64, "f32"), prompts, int(z["steps"]), nb)
+    assert tokens == z["tokens"].tolist()
