@@ -1,28 +1,33 @@
 """Benchmark of the paged-attention hot path on B200 (one JSON line on rank 0).
 
 Workload (the shape the north star's >=70 %-of-HBM target is quoted
-on): Llama-3-8B-shape GQA decode, 32 query heads / 8 KV heads / head_dim 128, bf16,
-32 layers, KV block size 16, a continuous batch of 256 sequences whose contexts are
-lognormal with mean 4096 clipped to 128..16384 (seed 0 per rank).  Synthetic data:
-pools, queries and new K/V rows are N(0,1); block tables are a seeded permutation of
-the pool (non-contiguous, unsorted).  The pools are real per-layer allocations
-(about 138 GB of KV for 32 layers), so every layer streams its own 4.3 GB from HBM;
-each layer's KV is far larger than the 126 MB L2, which is this benchmark's answer to
-L2 flushing.
+on): Llama-3-8B-shape GQA attention, 32 query heads / 8 KV heads / head_dim 128, bf16,
+32 layers, KV block size 16; a continuous batch of 256 sequences whose contexts are
+lognormal with mean 4096 clipped to 128..16384 (seed 0 per rank), with ~5 % per-step
+admit/evict churn whose new prompts (256..2048 tokens) run through varlen paged
+prefill.  Synthetic data: pools, queries and new K/V rows are N(0,1); block tables are a
+seeded permutation of the pool (non-contiguous, unsorted).  The pools are real
+per-layer allocations (about 140 GB of KV for 32 layers), so every layer streams its
+own ~4.3 GB from HBM; each layer's KV is far larger than the 126 MB L2, which is this
+benchmark's answer to L2 flushing.
 
-One step = one decode step of the hot path for the whole batch: the step's ragged
-metadata (planned on the host), then for each of the 32 layers the fused K+V append
-of the 256 new tokens and paged attention over every sequence's context (split-K
-decode + combine).  Contexts grow by one token per step, as in real decode.
+One step = what the reference's scheduler runs for that batch (it never mixes prefill
+and decode in one pass, inference_server/core/scheduler.py:425-437):
+  1. a prefill pass for the 13 newly admitted prompts — their metadata, then per layer
+     the fused K+V append of their tokens and tcgen05 varlen prefill attention;
+  2. a decode pass for all 256 sequences — metadata, then per layer the append of the
+     256 new tokens and split-K decode attention (tensor-pipe MMA) + combine.
+Decode contexts grow by one token per step.  Tokens generated per step: 256 + 13.
 
-* ``value``  decode tokens/s with inputs resident in HBM (per-step metadata uploaded
-  before the timed region), timed with CUDA events, max over ranks.
-* ``e2e``    the same through the public API with HOST buffers: every step plans its
-  metadata on the host and uploads it, copies each layer's q / new K / new V from pinned
-  host memory, and reads each layer's attention output back.
-* ``roofline``  the paged-attention launch (decode + combine) per layer: algorithmic
-  bytes (K+V of every context once, q and out, block ids, lengths) over its CUDA-event
-  duration, against the measured HBM copy peak.
+* ``value``  generated tokens/s with inputs resident in HBM (per-step metadata uploaded
+  before the timed region), CUDA events on the launching stream, max over ranks.
+* ``e2e``    the same through the public API with HOST buffers: every step plans and
+  uploads its metadata, copies each layer's q / new K / new V from pinned host memory
+  and reads each layer's attention output back.
+* ``roofline``  the decode attention launches (the dominant kernel): algorithmic bytes
+  (K+V of every context once, q and out, block ids, lengths) over their CUDA-event time,
+  against the measured HBM copy peak.  ``prefill_roofline``: the prefill attention
+  launches' causal FLOPs over their time, against the measured sustained bf16 peak.
 * ``cpu_baseline``  the CPU oracle (a numpy port of the reference's gather path) on a
   bounded sample of the same workload, on this host's cores.
 
@@ -50,6 +55,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "paged decode tok/s at 1/2/4/8 B200; paged-attn HBM GB/s vs 8 TB/s peak"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 NOMINAL_HBM_GBS = 8000.0
 
 
@@ -74,45 +80,64 @@ def clipped_lognormal_mu(mean: float, sigma: float, lo: float, hi: float) -> flo
 
 
 class Workload:
-    """The seeded decode batch of one rank."""
+    """The seeded batch of one rank: decode sequences plus per-step churn prompts."""
 
     def __init__(self, batch: int, layers: int, heads: int, kv_heads: int, head_dim: int, block_size: int,
-                 mean_ctx: float, lo: int, hi: int, sigma: float, seed: int, max_steps: int):
+                 mean_ctx: float, lo: int, hi: int, sigma: float, seed: int, max_steps: int, churn: float,
+                 prompt_lo: int = 256, prompt_hi: int = 2048):
         self.batch, self.layers, self.heads, self.kv_heads = batch, layers, heads, kv_heads
         self.head_dim, self.block_size = head_dim, block_size
         rng = np.random.default_rng(seed)
         mu = clipped_lognormal_mu(mean_ctx, sigma, lo, hi)
         self.ctx0 = np.clip(np.exp(rng.normal(mu, sigma, size=batch)), lo, hi).astype(np.int64)
         need = -(-(self.ctx0 + max_steps) // block_size)
-        self.num_blocks = int(need.sum()) + 16
+        self.n_churn = int(round(churn * batch))
+        churn_width = -(-prompt_hi // block_size)
+        self.num_blocks = int(need.sum()) + self.n_churn * churn_width + 16
         perm = rng.permutation(self.num_blocks)
         self.tables = np.zeros((batch, int(need.max())), dtype=np.int64)
         off = 0
         for i, n in enumerate(need):
             self.tables[i, :n] = perm[off:off + n]
             off += n
+        self.churn_tables = np.zeros((max(self.n_churn, 1), churn_width), dtype=np.int64)
+        for i in range(self.n_churn):
+            self.churn_tables[i] = perm[off:off + churn_width]
+            off += churn_width
         self.query_lens = np.ones(batch, dtype=np.int64)
+        # prompt lengths of every step's churn (uniform 256..2048, seeded)
+        self.prompts = rng.integers(prompt_lo, prompt_hi + 1, size=(max_steps, max(self.n_churn, 1)))
 
     def context_lens(self, step: int) -> np.ndarray:
         return self.ctx0 + step
 
+    def prompt_lens(self, step: int) -> np.ndarray:
+        return self.prompts[step, :self.n_churn].astype(np.int64)
+
     def attention_bytes(self, step: int, elem: int) -> int:
-        """Algorithmic HBM bytes of one layer's paged attention at `step`."""
+        """Algorithmic HBM bytes of one layer's decode attention at `step`."""
         ctx = self.context_lens(step)
         kv = int(ctx.sum()) * self.kv_heads * self.head_dim * 2 * elem
         qo = 2 * self.batch * self.heads * self.head_dim * elem
         ids = int((-(-ctx // self.block_size)).sum()) * 4
         return kv + qo + ids + 8 * self.batch
 
+    def prefill_flops(self, step: int) -> float:
+        """Causal attention FLOPs of one layer's prefill pass at `step`:
+        4 * Hq * D * sum over prompts of sum_{t<L} (t + 1)."""
+        lens = self.prompt_lens(step).astype(np.float64)
+        return float(4.0 * self.heads * self.head_dim * np.sum(lens * (lens + 1) / 2))
 
-def _measured_hbm() -> tuple[float, str]:
+
+def _measured_peaks() -> tuple[float, float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), float(d["bf16_tflops_sustained"]), "measured"
         except Exception:
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback"
 
 
 class ClockSampler:
@@ -125,6 +150,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.rows: list[list[str]] = []
 
     def __enter__(self):
         try:
@@ -137,7 +163,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.rows = []
         if self.proc is None:
             return False
         time.sleep(0.2)
@@ -154,27 +179,37 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
-        rows = getattr(self, "rows", [])
+        rows = self.rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows]
+        mx = [num(r[2]) for r in rows]
+        power = [num(r[3]) for r in rows]
         reasons = set()
         for r in rows:
             for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
                                  r[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
-        loaded = [s for s, p in zip(sm, power) if p > 0.5 * max(power)] if power else sm
-        return {"sm_mhz": statistics.median(loaded or sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows), "power_w_max": max(power) if power else None}
+        pw = [p for p in power if p is not None]
+        loaded = [s for s, p in zip(sm, power) if s is not None and p is not None and pw and p > 0.5 * max(pw)]
+        sm_ok = [s for s in sm if s is not None]
+        return {"sm_mhz": statistics.median(loaded or sm_ok) if sm_ok else None,
+                "sm_max_mhz": max([m for m in mx if m is not None], default=None),
+                "reasons": sorted(reasons), "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
 # ------------------------------------------------------------------ CPU legs (oracle)
 def _sample_for_cpu(wl: Workload, nseq: int, step: int, dtype: str, seed: int):
-    """A bounded sample of the workload for the CPU oracle: the first `nseq` sequences at
-    `step`, with their own blocks only (float32 arrays holding bf16 values)."""
+    """A bounded sample of the workload for the CPU oracle: the first `nseq` decode
+    sequences at `step`, with their own blocks only (float32 arrays holding bf16 values)."""
     g = torch.Generator().manual_seed(seed)
     ctx = wl.context_lens(step)[:nseq]
     need = -(-ctx // wl.block_size)
@@ -205,22 +240,29 @@ def _blas_threads() -> int:
         return 1
 
 
-def cpu_layer_seconds(wl: Workload, nseq: int, dtype: str, budget_s: float, min_reps: int = 2):
-    """Mean wall time of one layer of the oracle's decode step (KV append + gather-path
-    attention) on the sample, repeated until `budget_s` is spent."""
+def _oracle_layer_timer(wl: Workload, nseq: int):
+    """One layer of the oracle's decode step (KV append + gather-path attention) on a
+    sample of `nseq` sequences; returns a function that runs it and returns seconds."""
     from oracle import paged_attention_oracle as oracle
 
-    q, kp, vp, tables, ctx, ql, knew, vnew, slots = _sample_for_cpu(wl, nseq, 0, dtype, seed=1234)
+    q, kp, vp, tables, ctx, ql, knew, vnew, slots = _sample_for_cpu(wl, nseq, 0, "bf16", seed=1234)
     scale = wl.head_dim ** -0.5
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while len(times) < min_reps or time.perf_counter() < t_end:
+
+    def one():
         t0 = time.perf_counter()
         kp2 = oracle.kv_append(kp, slots, knew)
         vp2 = oracle.kv_append(vp, slots, vnew)
-        oracle.paged_attention_gather(q, kp2, vp2, tables, ctx, ql, scale, dtype)
-        times.append(time.perf_counter() - t0)
-    return float(np.mean(times)), len(times)
+        oracle.paged_attention_gather(q, kp2, vp2, tables, ctx, ql, scale, "bf16")
+        return time.perf_counter() - t0
+
+    return one, ctx
+
+
+def _cpu_sample_text(wl: Workload, nseq: int, ctx, reps: int) -> str:
+    return (f"{nseq} decode sequences of the workload (contexts {ctx.tolist()}), {reps} repetitions of one layer "
+            f"of the oracle's KV append + gather-path attention (bf16 emulated in float32 numpy), scaled to "
+            f"{wl.layers} layers and to decode tokens/s; churn prefill not included; host has "
+            f"{os.cpu_count()} CPUs")
 
 
 def run_reference(args, rank: int, world: int) -> None:
@@ -229,32 +271,19 @@ def run_reference(args, rank: int, world: int) -> None:
         return
     wl = _make_workload(args, rank, max_steps=1)
     nseq = args.cpu_sample_seqs
-    from oracle import paged_attention_oracle as oracle
-
-    q, kp, vp, tables, ctx, ql, knew, vnew, slots = _sample_for_cpu(wl, nseq, 0, "bf16", seed=1234)
-    scale = wl.head_dim ** -0.5
-
-    def one_step():
-        t0 = time.perf_counter()
-        kp2 = oracle.kv_append(kp, slots, knew)
-        vp2 = oracle.kv_append(vp, slots, vnew)
-        oracle.paged_attention_gather(q, kp2, vp2, tables, ctx, ql, scale, "bf16")
-        return time.perf_counter() - t0
-
+    one, ctx = _oracle_layer_timer(wl, nseq)
     for _ in range(args.warmup):
-        one_step()
-    times = [one_step() for _ in range(args.steps)]
+        one()
+    times = [one() for _ in range(args.steps)]
     sec_layer = float(np.mean(times))
     value = nseq / (sec_layer * wl.layers)
-    threads = _blas_threads()
-    sample = (f"{nseq} sequences (contexts {ctx.tolist()}) of the workload, one layer per step of the oracle's "
-              f"KV append + gather-path attention (bf16 emulated in float32 numpy), scaled to {wl.layers} layers")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_layer * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": _config(args, wl, world),
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": _blas_threads(), "kind": "port",
+                         "sample": _cpu_sample_text(wl, nseq, ctx, len(times))},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "host_cpus": os.cpu_count(),
     }
@@ -264,83 +293,119 @@ def run_reference(args, rank: int, world: int) -> None:
 # ------------------------------------------------------------------ GPU arm
 def _make_workload(args, rank: int, max_steps: int) -> Workload:
     return Workload(batch=args.batch, layers=args.layers, heads=32, kv_heads=8, head_dim=128, block_size=16,
-                    mean_ctx=4096.0, lo=128, hi=16384, sigma=0.9, seed=args.seed + rank, max_steps=max_steps)
+                    mean_ctx=4096.0, lo=128, hi=16384, sigma=0.9, seed=args.seed + rank, max_steps=max_steps,
+                    churn=args.churn)
 
 
 def _config(args, wl: Workload, world: int) -> dict:
     return {
-        "workload": "BASELINE config 3: Llama-3-8B-shape GQA paged decode (32 q / 8 kv heads, head_dim 128, "
-                    "bf16, 32 layers, block 16), batch 256, contexts lognormal mean 4096 clipped 128..16384",
+        "workload": "BASELINE config 3: Llama-3-8B-shape GQA paged attention (32 q / 8 kv heads, head_dim 128, "
+                    "bf16, 32 layers, block 16), batch 256, contexts lognormal mean 4096 clipped 128..16384, "
+                    f"{wl.n_churn} churn prompts of 256..2048 tokens per step through varlen paged prefill",
         "model": "llama3-8b-shape attention hot path (random-init)",
         "global_batch": wl.batch * world,
         "batch_per_gpu": wl.batch,
+        "churn_prompts_per_step": wl.n_churn,
         "layers": wl.layers,
         "heads": wl.heads, "kv_heads": wl.kv_heads, "head_dim": wl.head_dim, "block_size": wl.block_size,
         "sum_context_step0": int(wl.ctx0.sum()),
         "seq_len": "ragged (mean 4096)",
         "l2": "inputs larger than L2 (each layer's KV is ~4.3 GB vs 126 MB L2); no flush",
         "parallelism": f"replicas x{world} (request-level data parallel, no collectives)",
-        "step": "plan metadata, then per layer: fused K+V append of 256 new tokens + paged decode attention",
+        "step": "prefill pass for the churn prompts + decode pass for the batch; per layer: fused K+V append, "
+                "then paged attention",
     }
+
+
+class _Pass:
+    """Device-resident per-layer inputs of one pass (decode or prefill)."""
+
+    def __init__(self, L, tokens, Hq, Hkv, D, dtype, dev, g):
+        self.q = [torch.randn(tokens, Hq, D, generator=g, device=dev).to(dtype) for _ in range(L)]
+        self.k = [torch.randn(tokens, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
+        self.v = [torch.randn(tokens, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
 
 
 def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     from __graft_entry__ import import_package
 
     pkg = import_package()
+    lib = pkg._lib.lib()
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     steps_total = args.warmup + args.steps
     wl = _make_workload(args, rank, max_steps=steps_total + 1)
     L, B, Hq, Hkv, D, BS = wl.layers, wl.batch, wl.heads, wl.kv_heads, wl.head_dim, wl.block_size
-    dtype = torch.bfloat16
-    elem = 2
+    dtype, elem = torch.bfloat16, 2
+    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
+    sm = pkg.metadata.sm_count(dev)
 
     # ---- device-resident inputs
     g = torch.Generator(device=dev).manual_seed(args.seed + 100 * rank)
     pool_shape = (wl.num_blocks, BS, Hkv, D)
-    k_pools, v_pools = [], []
-    for _ in range(L):
-        k_pools.append(torch.empty(pool_shape, dtype=dtype, device=dev).normal_(generator=g))
-        v_pools.append(torch.empty(pool_shape, dtype=dtype, device=dev).normal_(generator=g))
-    q_dev = [torch.randn(B, Hq, D, generator=g, device=dev).to(dtype) for _ in range(L)]
-    k_new = [torch.randn(B, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
-    v_new = [torch.randn(B, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
-    bt_dev = torch.from_numpy(wl.tables).to(dev)
-    ql_dev = torch.from_numpy(wl.query_lens).to(dev)
+    k_pools = [torch.empty(pool_shape, dtype=dtype, device=dev).normal_(generator=g) for _ in range(L)]
+    v_pools = [torch.empty(pool_shape, dtype=dtype, device=dev).normal_(generator=g) for _ in range(L)]
+    dec = _Pass(L, B, Hq, Hkv, D, dtype, dev, g)
+    t_pre_max = max(int(wl.prompts[:, :wl.n_churn].sum(axis=1).max()), 1) if wl.n_churn else 1
+    pre = _Pass(L, t_pre_max, Hq, Hkv, D, dtype, dev, g)
+    bt_dec = torch.from_numpy(wl.tables).to(dev)
+    bt_pre = torch.from_numpy(wl.churn_tables).to(dev)
     scale = D ** -0.5
 
-    def plan(step: int, upload: bool = True):
-        ctx = wl.context_lens(step)
-        m = pkg.StepMetadata.plan_host(ctx, wl.query_lens, wl.tables, num_tokens=B,
-                                       pool_num_blocks=wl.num_blocks, block_size=BS, num_kv_heads=Hkv,
-                                       sm=pkg.metadata.sm_count(dev), pinned=True)
-        if upload:
-            m.upload(dev)
-        return m
+    def plan_decode(step: int):
+        m = pkg.StepMetadata.plan_host(wl.context_lens(step), wl.query_lens, wl.tables, num_tokens=B,
+                                       pool_num_blocks=wl.num_blocks, block_size=BS, num_kv_heads=Hkv, sm=sm,
+                                       prefill_tile_tokens=tile, pinned=True)
+        return m.upload(dev)
 
-    metas = [plan(s) for s in range(steps_total)]
-    ctx_dev = [torch.from_numpy(wl.context_lens(s)).to(dev) for s in range(steps_total)]
+    def plan_prefill(step: int):
+        lens = wl.prompt_lens(step)
+        m = pkg.StepMetadata.plan_host(lens, lens, wl.churn_tables[:wl.n_churn], num_tokens=int(lens.sum()),
+                                       pool_num_blocks=wl.num_blocks, block_size=BS, num_kv_heads=Hkv, sm=sm,
+                                       prefill_tile_tokens=tile, pinned=True)
+        return m.upload(dev)
+
+    metas_d = [plan_decode(s) for s in range(steps_total)]
+    metas_p = [plan_prefill(s) for s in range(steps_total)] if wl.n_churn else [None] * steps_total
+    dummy_lens = torch.zeros(1, dtype=torch.int64, device=dev)
     torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    launches = [0]
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
-    stream = torch.cuda.current_stream(dev)
-    launches_per_step = L * (2 + (1 if metas[0].plan.num_combine_seqs > 0 else 0))
-
-    def device_step(s: int, ev=None):
-        meta = metas[s]
-        bt = pkg.attach(bt_dev, meta)
+    def run_pass(meta, bt, inp, tokens, ev=None, q_src=None, kv_src=None, out_host=None):
+        """Per layer: fused append of the pass's new tokens, then attention."""
         slots = meta.slot_mapping()
+        bt = pkg.attach(bt, meta)
         for layer in range(L):
-            pkg.reshape_and_cache(k_new[layer], v_new[layer], k_pools[layer], v_pools[layer], slots)
+            if q_src is not None:   # e2e: this layer's inputs come from pinned host memory
+                inp.q[0][:tokens].copy_(q_src[0][:tokens], non_blocking=True)
+                inp.k[0][:tokens].copy_(kv_src[0][:tokens], non_blocking=True)
+                inp.v[0][:tokens].copy_(kv_src[1][:tokens], non_blocking=True)
+                q, k, v = inp.q[0][:tokens], inp.k[0][:tokens], inp.v[0][:tokens]
+            else:
+                q, k, v = inp.q[layer][:tokens], inp.k[layer][:tokens], inp.v[layer][:tokens]
+            pkg.reshape_and_cache(k, v, k_pools[layer], v_pools[layer], slots)
             if ev is not None:
                 ev[layer][0].record(stream)
-            pkg.paged_attention_cuda(q_dev[layer], k_pools[layer], v_pools[layer], bt, ctx_dev[s], ql_dev, scale)
+            out = pkg.paged_attention_cuda(q, k_pools[layer], v_pools[layer], bt, dummy_lens, dummy_lens, scale)
             if ev is not None:
                 ev[layer][1].record(stream)
+            launches[0] += 1 + bin(lib.pa_last_launches()).count("1")   # append + attention kernels
+            if out_host is not None:
+                out_host[:tokens].copy_(out, non_blocking=True)
+
+    def events():
+        return [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
+
+    def device_step(s: int, ev_d=None, ev_p=None):
+        if wl.n_churn:
+            mp = metas_p[s]
+            run_pass(mp, bt_pre, pre, mp.num_tokens, ev_p)
+        run_pass(metas_d[s], bt_dec, dec, B, ev_d)
 
     clocks = ClockSampler(dev.index)
     with clocks:
@@ -349,50 +414,53 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
             device_step(s)
         barrier()
         torch.cuda.synchronize(dev)
+        launches[0] = 0
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        layer_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
-                        for _ in range(args.steps)]
+        ev_d = [events() for _ in range(args.steps)]
+        ev_p = [events() for _ in range(args.steps)]
         start.record(stream)
         for k in range(args.steps):
-            device_step(args.warmup + k, layer_events[k])
+            device_step(args.warmup + k, ev_d[k], ev_p[k])
         end.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
+        gpu_launches = launches[0]
         elapsed_ms = start.elapsed_time(end)
-        attn_ms = [layer_events[k][l][0].elapsed_time(layer_events[k][l][1])
-                   for k in range(args.steps) for l in range(L)]
+        dec_ms = [ev_d[k][l][0].elapsed_time(ev_d[k][l][1]) for k in range(args.steps) for l in range(L)]
+        pre_ms = ([ev_p[k][l][0].elapsed_time(ev_p[k][l][1]) for k in range(args.steps) for l in range(L)]
+                  if wl.n_churn else [0.0])
 
         # ---- e2e: host buffers through the public API
-        q_host = [t.cpu().pin_memory() for t in q_dev]
-        k_host = [t.cpu().pin_memory() for t in k_new]
-        v_host = [t.cpu().pin_memory() for t in v_new]
-        out_host = [torch.empty(B, Hq, D, dtype=dtype).pin_memory() for _ in range(L)]
-        q_buf = [torch.empty_like(t) for t in q_dev]
-        k_buf = [torch.empty_like(t) for t in k_new]
-        v_buf = [torch.empty_like(t) for t in v_new]
-        ctx_host = [torch.from_numpy(wl.context_lens(s)) for s in range(steps_total)]
-        meta_bytes = []
+        q_host_d = [dec.q[0].cpu().pin_memory()]
+        kv_host_d = [dec.k[0].cpu().pin_memory(), dec.v[0].cpu().pin_memory()]
+        out_host_d = torch.empty(B, Hq, D, dtype=dtype).pin_memory()
+        q_host_p = [pre.q[0].cpu().pin_memory()]
+        kv_host_p = [pre.k[0].cpu().pin_memory(), pre.v[0].cpu().pin_memory()]
+        out_host_p = torch.empty(t_pre_max, Hq, D, dtype=dtype).pin_memory()
+        h2d_bytes, d2h_bytes = [], []
 
         def e2e_step(s: int):
-            meta = plan(s)            # host planning + one metadata upload
-            meta_bytes.append(int(meta.plan.words) * 4)
-            bt = pkg.attach(bt_dev, meta)
-            slots = meta.slot_mapping()
-            for layer in range(L):
-                q_buf[layer].copy_(q_host[layer], non_blocking=True)
-                k_buf[layer].copy_(k_host[layer], non_blocking=True)
-                v_buf[layer].copy_(v_host[layer], non_blocking=True)
-                pkg.reshape_and_cache(k_buf[layer], v_buf[layer], k_pools[layer], v_pools[layer], slots)
-                out = pkg.paged_attention_cuda(q_buf[layer], k_pools[layer], v_pools[layer], bt, ctx_host[s],
-                                               ctx_host[s], scale)
-                out_host[layer].copy_(out, non_blocking=True)
+            h2d = d2h = 0
+            if wl.n_churn:
+                mp = plan_prefill(s)
+                tp = mp.num_tokens
+                run_pass(mp, bt_pre, pre, tp, q_src=q_host_p, kv_src=kv_host_p, out_host=out_host_p)
+                h2d += int(mp.plan.words) * 4 + L * tp * (Hq + 2 * Hkv) * D * elem
+                d2h += L * tp * Hq * D * elem
+            md = plan_decode(s)
+            run_pass(md, bt_dec, dec, B, q_src=q_host_d, kv_src=kv_host_d, out_host=out_host_d)
+            h2d += int(md.plan.words) * 4 + L * B * (Hq + 2 * Hkv) * D * elem
+            d2h += L * B * Hq * D * elem
+            h2d_bytes.append(h2d)
+            d2h_bytes.append(d2h)
 
         for s in range(args.warmup):
             e2e_step(s)
         barrier()
         torch.cuda.synchronize(dev)
+        h2d_bytes.clear()
+        d2h_bytes.clear()
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        meta_bytes.clear()
         e_start.record(stream)
         for k in range(args.steps):
             e2e_step(args.warmup + k)
@@ -403,52 +471,60 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     assert pkg.read_device_error(dev) == 0, "a kernel set the device error word"
 
     # ---- max over ranks
-    times = torch.tensor([elapsed_ms, e2e_ms, float(np.mean(attn_ms))], dtype=torch.float64, device=dev)
+    times = torch.tensor([elapsed_ms, e2e_ms, float(np.mean(dec_ms)), float(np.mean(pre_ms))],
+                         dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, attn_avg_ms = times.tolist()
+    elapsed_ms, e2e_ms, dec_avg_ms, pre_avg_ms = times.tolist()
     if rank != 0:
         return
 
-    tokens = B * args.steps * world
+    tokens = (B + wl.n_churn) * args.steps * world
     value = tokens / (elapsed_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
-    bytes_per_call = float(np.mean([wl.attention_bytes(args.warmup + k, elem) for k in range(args.steps)]))
-    achieved = bytes_per_call / (attn_avg_ms / 1e3) / 1e9
-    peak, peak_kind = _measured_hbm()
-    traffic = _traffic_per_call(float(np.mean([wl.context_lens(args.warmup + k).sum()
-                                               for k in range(args.steps)])))
+    timed = [args.warmup + k for k in range(args.steps)]
+    bytes_per_call = float(np.mean([wl.attention_bytes(s, elem) for s in timed]))
+    achieved = bytes_per_call / (dec_avg_ms / 1e3) / 1e9
+    hbm_peak, bf16_peak, peak_kind = _measured_peaks()
+    traffic = _traffic_per_call(float(np.mean([wl.context_lens(s).sum() for s in timed])))
+    pre_flops = float(np.mean([wl.prefill_flops(s) for s in timed])) if wl.n_churn else 0.0
+    pre_tflops = pre_flops / (pre_avg_ms / 1e3) / 1e12 if wl.n_churn else None
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        sec_layer, reps = cpu_layer_seconds(wl, args.cpu_sample_seqs, "bf16", args.cpu_budget_s)
-        cpu = {"value": args.cpu_sample_seqs / (sec_layer * L), "unit": "tok/s", "cores": _blas_threads(),
-               "kind": "port",
-               "sample": f"{args.cpu_sample_seqs} sequences of the workload (contexts "
-                         f"{wl.context_lens(0)[:args.cpu_sample_seqs].tolist()}), {reps} repetitions of one layer "
-                         f"of the oracle's KV append + gather-path attention (bf16 emulated in float32 numpy), "
-                         f"scaled to {L} layers; host has {os.cpu_count()} CPUs"}
+        one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs)
+        one()
+        t_end = time.perf_counter() + args.cpu_budget_s
+        reps = []
+        while len(reps) < 2 or time.perf_counter() < t_end:
+            reps.append(one())
+        cpu = {"value": args.cpu_sample_seqs / (float(np.mean(reps)) * L), "unit": "tok/s", "cores": _blas_threads(),
+               "kind": "port", "sample": _cpu_sample_text(wl, args.cpu_sample_seqs, ctx, len(reps))}
 
-    h2d = float(np.mean(meta_bytes)) + L * (q_host[0].numel() + 2 * k_host[0].numel()) * elem
-    d2h = L * out_host[0].numel() * elem
+    source = "MEASURED_PEAKS.json" if peak_kind == "measured" else "fallback"
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": _config(args, wl, world),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6.65 TB/s",
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy ({source} hbm_gbs)",
                      "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS, "traffic": traffic,
-                     "kernel": "paged attention per layer (split-K decode + combine)",
-                     "algorithmic_bytes_per_launch": bytes_per_call, "avg_launch_ms": attn_avg_ms},
+                     "kernel": "decode paged attention per layer (tensor-pipe split-K decode + combine)",
+                     "algorithmic_bytes_per_launch": bytes_per_call, "avg_launch_ms": dec_avg_ms},
+        "prefill_roofline": None if not wl.n_churn else {
+            "bound": "tensor", "achieved": pre_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
+            "frac": pre_tflops / bf16_peak, "peak_source": f"{peak_kind} sustained bf16 ({source})",
+            "kernel": "prefill paged attention per layer (tcgen05 varlen prefill)",
+            "causal_flops_per_launch": pre_flops, "avg_launch_ms": pre_avg_ms,
+            "prompt_tokens_per_step": float(np.mean([wl.prompt_lens(s).sum() for s in timed]))},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "ms_per_step": e2e_ms / args.steps},
-        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(np.mean(h2d_bytes)),
+                "d2h_bytes_per_step": int(np.mean(d2h_bytes)), "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": gpu_launches,
         "clocks": clocks.summary(),
-        "decode_splits": {"split_blocks": metas[0].plan.split_blocks, "items": metas[0].plan.num_decode_items,
-                          "combine_seqs": metas[0].plan.num_combine_seqs},
+        "decode_splits": {"split_blocks": metas_d[0].plan.split_blocks, "items": metas_d[0].plan.num_decode_items,
+                          "combine_seqs": metas_d[0].plan.num_combine_seqs},
     }
     print(json.dumps(line), flush=True)
 
@@ -476,6 +552,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--churn", type=float, default=0.05, help="fraction of the batch re-admitted per step")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-seqs", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)

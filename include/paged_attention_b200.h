@@ -81,6 +81,16 @@ int32_t pa_abi_version(void);
 /* Message of the calling thread's last failed call ("" if none). */
 const char* pa_last_error(void);
 
+/* Kernels launched by the calling thread's most recent pa_paged_attention_fwd or
+ * pa_paged_attention_fwd_noalloc call (a bit mask of PA_LAUNCH_*); lets tests and
+ * benchmarks confirm which kernel served which rows.  No counterpart in the reference. */
+#define PA_LAUNCH_DECODE_MMA 1      /* tensor-pipe split-K decode (bf16/fp16) */
+#define PA_LAUNCH_DECODE_SIMT 2     /* SIMT split-K decode */
+#define PA_LAUNCH_COMBINE 4         /* split-K combine */
+#define PA_LAUNCH_PREFILL_TC 8      /* tcgen05 varlen prefill */
+#define PA_LAUNCH_GENERIC 16        /* generic ragged kernel */
+int32_t pa_last_launches(void);
+
 /*
  * Upper bound on the int32 words pa_plan_step writes for a step with num_seqs
  * sequences, num_tokens packed tokens and at most max_blocks_per_seq blocks per row.

@@ -29,6 +29,12 @@ PA_DTYPE_BF16 = 2
 
 PA_NOALLOC_SCRATCH_BYTES = 32 << 20
 
+PA_LAUNCH_DECODE_MMA = 1
+PA_LAUNCH_DECODE_SIMT = 2
+PA_LAUNCH_COMBINE = 4
+PA_LAUNCH_PREFILL_TC = 8
+PA_LAUNCH_GENERIC = 16
+
 ABI_VERSION = 1
 
 
@@ -70,6 +76,7 @@ class StepPlan(ctypes.Structure):
 
 _SIGNATURES = {
     "pa_abi_version": (c_int32, []),
+    "pa_last_launches": (c_int32, []),
     "pa_last_error": (c_char_p, []),
     "pa_plan_words_bound": (c_int64, [c_int32, c_int32, c_int32]),
     "pa_plan_step": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int64,
@@ -117,6 +124,14 @@ def declared_symbols() -> list[str]:
     """Every function the public header declares."""
     text = HEADER.read_text()
     return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(pa_\w+)\s*\(", text, flags=re.M)))
+
+
+def last_launches() -> set[str]:
+    """Names of the kernels the calling thread's last attention call launched."""
+    mask = lib().pa_last_launches()
+    names = {PA_LAUNCH_DECODE_MMA: "decode_mma", PA_LAUNCH_DECODE_SIMT: "decode_simt",
+             PA_LAUNCH_COMBINE: "combine", PA_LAUNCH_PREFILL_TC: "prefill_tc", PA_LAUNCH_GENERIC: "generic"}
+    return {n for bit, n in names.items() if mask & bit}
 
 
 def check(rc: int) -> None:

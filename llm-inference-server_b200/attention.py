@@ -20,7 +20,7 @@ import os
 import torch
 
 from . import _lib
-from .metadata import StepMetadata, attached, sm_count
+from .metadata import StepMetadata, attached, prefill_tile_tokens, sm_count
 
 _DTYPE_CODE = {torch.float32: _lib.PA_DTYPE_F32, torch.float16: _lib.PA_DTYPE_F16,
                torch.bfloat16: _lib.PA_DTYPE_BF16}
@@ -105,7 +105,8 @@ def step_metadata_for(query, k_pool, block_tables, context_lens, query_lens) -> 
         return meta
     return StepMetadata.build(context_lens, query_lens, block_tables, num_tokens=query.shape[0],
                               pool_num_blocks=num_blocks, block_size=block_size, num_kv_heads=kv_heads,
-                              device=query.device)
+                              device=query.device,
+                              prefill_tile_tokens=prefill_tile_tokens(query.shape[1], kv_heads))
 
 
 def paged_attention_cuda(query, k_pool, v_pool, block_tables, context_lens, query_lens, scale):

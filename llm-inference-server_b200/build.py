@@ -25,7 +25,7 @@ BUILD = PKG / "_build"
 LIB_NAME = "libpaged_attn_b200.so"
 LIB = PKG / LIB_NAME
 
-CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "attention_generic.cu", "kv_append.cu",
+CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "prefill_tc.cu", "attention_generic.cu", "kv_append.cu",
               "attention_noalloc.cu"]
 CXX_SOURCES = ["step_plan.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

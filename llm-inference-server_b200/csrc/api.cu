@@ -97,6 +97,8 @@ static int32_t pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int
   return PA_OK;
 }
 
+static thread_local int32_t g_last_launches = 0;
+
 static int32_t cuda_fail(cudaError_t e, const char* what) {
   return fail(PA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
@@ -104,6 +106,8 @@ static int32_t cuda_fail(cudaError_t e, const char* what) {
 }  // namespace pa
 
 extern "C" {
+
+int32_t pa_last_launches(void) { return pa::g_last_launches; }
 
 uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim) {
   if (!plan) return 0;
@@ -122,6 +126,7 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
                                int64_t out_stride_head, void* workspace, uint64_t workspace_bytes,
                                void* stream_ptr) {
   using namespace pa;
+  g_last_launches = 0;
   if (!plan) return fail(PA_ERR_INVALID_ARGUMENT, "plan must not be NULL");
   if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
     return fail(PA_ERR_UNSUPPORTED, "dtype code %d is not float32, float16 or bfloat16", dtype);
@@ -197,6 +202,7 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
     cudaError_t e = use_mma ? launch_decode_mma(dtype, head_dim, group, tk, tv, p, stream)
                             : launch_decode(dtype, head_dim, group, tk, tv, p, stream);
     if (e != cudaSuccess) return cuda_fail(e, "split-K decode launch");
+    if (p.num_items > 0) g_last_launches |= use_mma ? PA_LAUNCH_DECODE_MMA : PA_LAUNCH_DECODE_SIMT;
     if (plan->num_combine_seqs > 0) {
       CombineParams c{};
       c.out = out;
@@ -210,10 +216,51 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
       c.head_dim = head_dim;
       e = launch_combine(dtype, c, stream);
       if (e != cudaSuccess) return cuda_fail(e, "split-K combine launch");
+      g_last_launches |= PA_LAUNCH_COMBINE;
     }
   }
-  const bool rest = fast_decode ? plan->num_prefill_tokens > 0 : true;
-  if (rest) {
+  // Prefill rows go to the tcgen05 kernel when the plan was tiled for this head shape
+  // (128 / G query tokens per tile) and query/out rows are 16-byte aligned.
+  const int es = elem_size(dtype);
+  const bool tc_prefill = plan->num_prefill_tiles > 0 && prefill_tc_supported(dtype, head_dim, group, block_size) &&
+                          plan->prefill_tile_tokens * group == prefill_tile_rows() && q_stride_dim == 1 &&
+                          (q_stride_token * es) % 16 == 0 && (q_stride_head * es) % 16 == 0 &&
+                          reinterpret_cast<uintptr_t>(query) % 16 == 0 && (out_stride_token * es) % 16 == 0 &&
+                          (out_stride_head * es) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                          reinterpret_cast<uintptr_t>(k_pool) % 16 == 0 &&
+                          reinterpret_cast<uintptr_t>(v_pool) % 16 == 0;
+  if (tc_prefill) {
+    CUtensorMap tk, tv;
+    int32_t rc = pool_tensor_map(k_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, 64, true, &tk);
+    if (rc != PA_OK) return rc;
+    rc = pool_tensor_map(v_pool, pool_num_blocks, block_size, num_kv_heads, head_dim, dtype, 64, true, &tv);
+    if (rc != PA_OK) return rc;
+    PrefillParams f{};
+    f.q = query;
+    f.q_st = q_stride_token;
+    f.q_sh = q_stride_head;
+    f.out = out;
+    f.o_st = out_stride_token;
+    f.o_sh = out_stride_head;
+    f.tables = tables;
+    f.width = plan->table_width;
+    f.ctx_lens = meta + plan->off_context_lens;
+    f.query_lens = meta + plan->off_query_lens;
+    f.cu_q = meta + plan->off_cu_query_lens;
+    f.tiles = reinterpret_cast<const int2*>(meta + plan->off_prefill_tiles);
+    f.num_tiles = plan->num_prefill_tiles;
+    f.num_heads = num_heads;
+    f.num_kv_heads = num_kv_heads;
+    f.pool_blocks = int32_t(pool_num_blocks);
+    f.qscale = qscale;
+    f.err = err;
+    cudaError_t e = launch_prefill_tc(dtype, head_dim, group, tk, tv, f, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 prefill launch");
+    g_last_launches |= PA_LAUNCH_PREFILL_TC;
+  }
+  const bool decode_left = plan->num_decode_seqs > 0 && !fast_decode;
+  const bool prefill_left = plan->num_prefill_tokens > 0 && !tc_prefill;
+  if (decode_left || prefill_left) {
     GenericParams g{};
     g.q = query;
     g.q_st = q_stride_token;
@@ -234,12 +281,14 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
     g.q_pos = meta + plan->off_q_pos;
     g.query_lens = meta + plan->off_query_lens;
     g.num_tokens = num_tokens;
-    g.skip_decode = fast_decode ? 1 : 0;
+    g.skip_decode = decode_left ? 0 : 1;
+    g.skip_prefill = prefill_left ? 0 : 1;
     g.pool_blocks = pool_num_blocks;
     g.qscale = qscale;
     g.err = err;
     cudaError_t e = launch_generic(dtype, g, stream);
     if (e != cudaSuccess) return cuda_fail(e, "generic attention launch");
+    g_last_launches |= PA_LAUNCH_GENERIC;
   }
   return PA_OK;
 }

@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(32 * kGenericWarps) paged_attention_generic_ke
   const int tok = int(pair / p.num_heads), h = int(pair % p.num_heads);
   const int seq = p.seq_idx[tok];
   if (p.skip_decode && p.query_lens[seq] == 1) return;
+  if (p.skip_prefill && p.query_lens[seq] > 1) return;
   const int n_keys = p.q_pos[tok] + 1;
   const int kvh = h / (p.num_heads / p.num_kv_heads);
   const int D = p.head_dim;

@@ -57,7 +57,27 @@ struct GenericParams {
   const int32_t* query_lens;
   int32_t num_tokens;
   int32_t skip_decode;        // 1: tokens of query_len == 1 sequences are done elsewhere
+  int32_t skip_prefill;       // 1: tokens of query_len > 1 sequences are done elsewhere
   int64_t pool_blocks;
+  float qscale;
+  int* err;
+};
+
+// tcgen05 varlen prefill over (sequence, first query row) tiles, one CTA per tile and KV head.
+struct PrefillParams {
+  const void* q;
+  int64_t q_st, q_sh;         // element strides of query (unit stride along head_dim)
+  void* out;
+  int64_t o_st, o_sh;
+  const int32_t* tables;      // [B, width]
+  int32_t width;
+  const int32_t* ctx_lens;    // [B]
+  const int32_t* query_lens;  // [B]
+  const int32_t* cu_q;        // [B+1]
+  const int2* tiles;          // [num_tiles] seq, first query row
+  int32_t num_tiles;
+  int32_t num_heads, num_kv_heads;
+  int32_t pool_blocks;
   float qscale;
   int* err;
 };
@@ -87,6 +107,11 @@ bool decode_mma_supported(int dtype, int head_dim, int group, int block_size);
 cudaError_t launch_decode_mma(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
                               const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_generic(int dtype, const GenericParams& p, cudaStream_t stream);
+// tcgen05 prefill (bf16/fp16): tiles of prefill_tile_rows() (token, head) rows.
+bool prefill_tc_supported(int dtype, int head_dim, int group, int block_size);
+int prefill_tile_rows();
+cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
+                              const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 
 }  // namespace pa

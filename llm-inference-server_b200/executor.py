@@ -34,7 +34,7 @@ from transformers import AttentionInterface, Cache
 
 from .attention import paged_attention_cuda
 from .kv_cache import reshape_and_cache
-from .metadata import StepMetadata, attach
+from .metadata import StepMetadata, attach, prefill_tile_tokens
 
 #: Name under which the CUDA attention is registered with transformers while a paged
 #: forward runs (prefixed so it cannot collide with transformers' own entries).
@@ -103,6 +103,9 @@ class CudaPagedExecutor:
         if self.device.type != "cuda":
             raise NotImplementedError(f"ATTENTION=cuda: the paged executor needs a CUDA device, got {self.device}")
         self.num_blocks, self.block_size, self.num_kv_heads, _ = pool.k[0].shape
+        cfg = model.config
+        heads = getattr(cfg, "num_attention_heads", None) or cfg.n_head
+        self.tile_tokens = prefill_tile_tokens(heads, self.num_kv_heads)
 
     @torch.inference_mode()
     def execute(self, seqs) -> list[int]:
@@ -148,7 +151,8 @@ class CudaPagedExecutor:
         for i, r in enumerate(rows):
             tables[i, :len(r)] = r
         meta = StepMetadata.build(c_lens, q_lens, tables, num_tokens=len(ids), pool_num_blocks=self.num_blocks,
-                                  block_size=bs, num_kv_heads=self.num_kv_heads, device=self.device)
+                                  block_size=bs, num_kv_heads=self.num_kv_heads, device=self.device,
+                                  prefill_tile_tokens=self.tile_tokens)
         dev = self.device
         block_tables = attach(torch.empty(len(seqs), meta.plan.table_width, dtype=torch.long, device=dev), meta)
         buf = meta.device_buffer

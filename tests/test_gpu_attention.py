@@ -95,7 +95,9 @@ def test_fast_and_generic_kernels_agree(pkg):
     odd.copy_(q_dev)
     assert odd.stride(2) == 2
     fast = pkg.paged_attention_cuda(q_dev, kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.088)
+    assert pkg._lib.last_launches() <= {"decode_simt", "combine"}
     slow = pkg.paged_attention_cuda(odd, kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), 0.088)
+    assert pkg._lib.last_launches() == {"generic"}
     torch.testing.assert_close(fast, slow, atol=2e-6, rtol=2e-6)
 
 
@@ -179,9 +181,54 @@ def test_tensor_pipe_and_simt_decode_agree(pkg, oracle, dtype, heads, kv_heads, 
     assert odd.stride(1) % 2 == 1 and odd.stride(2) == 1
     args = (kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
     mma = pkg.paged_attention_cuda(qd, *args).float().cpu().numpy()
+    assert "decode_mma" in pkg._lib.last_launches() and "decode_simt" not in pkg._lib.last_launches()
     simt = pkg.paged_attention_cuda(odd, *args).float().cpu().numpy()
+    assert "decode_simt" in pkg._lib.last_launches() and "decode_mma" not in pkg._lib.last_launches()
     ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
                                         cl.numpy(), ql.numpy(), d ** -0.5, dtype)
     _close(mma, ref, dtype, "tensor-pipe decode")
     _close(simt, ref, dtype, "SIMT decode")
     np.testing.assert_allclose(mma, simt, atol=1e-2, rtol=1e-2)
+
+
+PREFILL_LENGTHS = [(300, 300), (129, 129), (16, 16), (17, 17), (200, 57), (700, 700), (513, 100), (40, 3),
+                   (5, 5), (130, 2), (256, 256), (1, 1), (90, 1)]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("heads,kv_heads,d", [(32, 8, 128), (64, 8, 128), (12, 12, 64), (16, 8, 64), (8, 4, 128)])
+def test_tensor_core_prefill_matches_oracle(pkg, oracle, dtype, heads, kv_heads, d):
+    """Varlen paged prefill on tcgen05 for GQA groups 1/2/4/8 and head_dims 64/128:
+    prompts shorter and longer than a tile, prefix-cache hits (query shorter than the
+    context), contexts that end mid-block and mid-KV-tile, plus decode rows in the same
+    call.  A query with an odd head stride sends the same rows through the generic
+    kernel, which must agree."""
+    q, kp, vp, bt, cl, ql = ragged_batch(PREFILL_LENGTHS, bs=16, d=d, heads=heads, kv_heads=kv_heads,
+                                         dtype=DT[dtype], seed=11)
+    qd = q.to(DEV)
+    args = (kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
+    tc = pkg.paged_attention_cuda(qd, *args).float().cpu().numpy()
+    assert {"prefill_tc", "decode_mma"} <= pkg._lib.last_launches() <= {"prefill_tc", "decode_mma", "combine"}
+    odd = torch.empty(q.shape[0], q.shape[1], d + 1, dtype=qd.dtype, device=DEV)[:, :, :d]
+    odd.copy_(qd)
+    generic = pkg.paged_attention_cuda(odd, *args).float().cpu().numpy()
+    assert {"generic", "decode_simt"} <= pkg._lib.last_launches() <= {"generic", "decode_simt", "combine"}
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), d ** -0.5, dtype)
+    _close(tc, ref, dtype, "tcgen05 prefill")
+    _close(generic, ref, dtype, "generic prefill")
+    assert pkg.read_device_error() == 0
+
+
+def test_tensor_core_prefill_churn_shape(pkg, oracle):
+    """BASELINE config 3's churn prompts (256..2048 tokens) at the Llama-8B shape: 3
+    prompts through the tcgen05 kernel, one re-computed by the oracle."""
+    rng = np.random.default_rng(5)
+    lengths = [(int(n), int(n)) for n in rng.integers(256, 2049, size=3)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=32, kv_heads=8, dtype=torch.bfloat16, seed=3)
+    out = _run(pkg, q, kp, vp, bt, cl, ql, 128 ** -0.5).float().cpu().numpy()
+    assert pkg._lib.last_launches() == {"prefill_tc"}
+    pick = [int(np.argmin([c for c, _ in lengths]))]
+    sub = compact_subbatch(q, kp, vp, bt, cl, ql, lengths, pick, 16)
+    ref = oracle.paged_attention_gather(*sub, 128 ** -0.5, "bf16")
+    _close(out[subset_rows(lengths, pick)], ref, "bf16")
