@@ -8,20 +8,24 @@
 // Work: one CTA per (prefill tile, KV head).  A tile is 128 // G consecutive query
 // tokens of one sequence; its 128 rows are the (token, query head) pairs of those tokens
 // and the G = Hq / Hkv query heads sharing the KV head (row r = token r / G, head r % G),
-// so every K/V byte a CTA loads serves all G heads.  KV is walked in tiles of 128 keys
-// (8 pool blocks) up to the causal limit of the tile's last token.
+// so every K/V byte a CTA loads serves all G heads.  KV is walked in tiles of 64 keys
+// (4 pool blocks) up to the causal limit of the tile's last token.  The footprint
+// (112 KB of shared memory and 256 TMEM columns at head_dim 128) lets two CTAs share an
+// SM, so one CTA's softmax and latencies overlap the other's MMAs.
 //
 // Roles (192 threads):
-//   warps 0-3  one thread per row: stage Q, softmax, O rescale, epilogue.  Row r lives in
-//              TMEM lane r, so row max and row sum are thread-local.
-//   warp 4     TMA producer: per KV tile, 8 blocks x (head_dim/64) boxes of K and of V
+//   warps 0-3  one thread per row: stage Q (overlapping the first K/V loads), softmax,
+//              O rescale, epilogue.  Row r lives in TMEM lane r, so row max and row sum
+//              are thread-local.
+//   warp 4     TMA producer: per KV tile, 4 blocks x (head_dim/64) boxes of K and of V
 //              (128-byte swizzle) into a 2-stage ring; block ids come from the table.
-//   warp 5     allocates TMEM (S: 128 columns, O: head_dim columns) and issues MMAs:
-//              S = Q.K^T (M=128, N=128, K=16 per instruction; Q and K K-major) and
+//   warp 5     allocates TMEM (S: 64 columns, O: head_dim columns) and issues MMAs:
+//              S = Q.K^T (M=128, N=64, K=16 per instruction; Q and K K-major) and
 //              O += P.V (M=128, N=head_dim; P K-major from shared memory, V MN-major).
 // Per KV tile j: TMA(K_j,V_j) -> MMA S_j -> softmax j reads S (s_consumed) while MMA
 // may already start S_{j+1} -> softmax waits PV_{j-1}, writes P_j (bf16/fp16, swizzled)
-// and rescales O in TMEM by exp2(m_old - m_new) -> MMA PV_j.  Scores, softmax and the
+// and rescales O in TMEM by exp2(m_old - m_new) (skipped when no row maximum of the warp
+// moved) -> MMA PV_j.  Scores, softmax and the
 // O accumulator are float32; P is rounded to the pool dtype as the reference rounds its
 // probabilities to the V dtype before P.V (attention.py:184-185).
 //
@@ -35,33 +39,41 @@
 namespace pa {
 
 constexpr int kPfRows = 128;
-constexpr int kPfKeys = 128;
+constexpr int kPfKeys = 64;
 constexpr int kPfBlocks = kPfKeys / 16;
 constexpr int kPfStages = 2;
 constexpr int kPfThreads = 192;
 constexpr int kPfSwHalf = kPfRows * 128;  // one 64-element-wide swizzled column half of a 128-row tile
-constexpr uint32_t kPfTmemCols = 256;
+constexpr int kPfKvHalf = kPfKeys * 128;  // the same for a 64-key K or V tile
+constexpr float kLazyRescale = 8.f;        // raise the running row max only past 2^8 headroom
 
 template <int D>
 struct PfCfg {
   static constexpr int NH = D / 64;
   static constexpr int Q_BYTES = NH * kPfSwHalf;
-  static constexpr int P_BYTES = 2 * kPfSwHalf;
-  static constexpr int K_BYTES = NH * kPfSwHalf;
+  static constexpr int P_BYTES = kPfSwHalf;          // 128 rows x 64 keys
+  static constexpr int K_BYTES = NH * kPfKvHalf;
   static constexpr int STAGE = 2 * K_BYTES;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_P = OFF_Q + Q_BYTES;
   static constexpr int OFF_ST = OFF_P + P_BYTES;
   static constexpr int OFF_BAR = OFF_ST + kPfStages * STAGE;
   static constexpr int SMEM = OFF_BAR + 128;
+  static constexpr uint32_t TMEM_COLS = (kPfKeys + D) <= 128 ? 128u : 256u;  // S then O
 };
 
 struct PfBars {
   uint64_t kv_full[kPfStages];
   uint64_t kv_empty[kPfStages];
-  uint64_t s_full, s_consumed, p_ready, pv_done;
+  uint64_t q_full, s_full, s_consumed, p_ready, pv_done;
   uint32_t tmem_base;
 };
+
+__device__ __forceinline__ float ex2(float x) {  // the hardware base-2 exponential
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -83,7 +95,7 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 }
 
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __launch_bounds__(kPfThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                             const PrefillParams p) {
   using C = PfCfg<D>;
@@ -107,7 +119,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int32_t* trow = p.tables + int64_t(seq) * p.width;
 
   if (warp == 5) {
-    tmem_alloc(&bars->tmem_base, kPfTmemCols);
+    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -115,12 +127,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
     }
+    mbar_init(&bars->q_full, 128);
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->s_consumed, 128);
     mbar_init(&bars->p_ready, 128);
     mbar_init(&bars->pv_done, 1);
     fence_mbar_init();
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  const uint32_t tS = tbase, tO = tbase + kPfKeys;
+  bool ok = true;
 
   // Row of this thread (softmax warps): token t = r / G, query head kvh*G + r % G.
   const int r = tid;
@@ -128,22 +147,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const bool row_valid = tid < kPfRows && t_row < ntok;
   const int t_eff = min(t_row, ntok - 1);
   const int qpos = ctx - ql + t0 + t_eff;
-  if (tid < kPfRows) {  // stage Q (zeros for rows past the tile's tokens)
-    const T* src = static_cast<const T*>(p.q) + int64_t(tokbase + t0 + t_eff) * p.q_st +
-                   int64_t(kvh * G + g_row) * p.q_sh;
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      uint4 v = row_valid ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(sQ + (c >> 3) * kPfSwHalf + sw_off(r, c & 7)) = v;
-    }
-    fence_proxy_async_smem();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = bars->tmem_base;
-  const uint32_t tS = tbase, tO = tbase + 128;
-  bool ok = true;
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
@@ -170,8 +173,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
 #pragma unroll
           for (int h = 0; h < NH; ++h) {
-            tma_load_3d(kst + h * kPfSwHalf + b * 2048, &tk, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
-            tma_load_3d(vst + h * kPfSwHalf + b * 2048, &tv, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
+            tma_load_3d(kst + h * kPfKvHalf + b * 2048, &tk, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
+            tma_load_3d(vst + h * kPfKvHalf + b * 2048, &tv, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
           }
         }
       }
@@ -188,14 +191,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t v0 = smem_u32(sST + (i % kPfStages) * C::STAGE + C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-          const uint64_t a = smem_desc_sw128(p0 + (kk >> 2) * kPfSwHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = smem_desc_sw128(v0 + kk * 2048, kPfSwHalf, 1024);
+          const uint64_t a = smem_desc_sw128(p0 + kk * 32, 16, 1024);
+          const uint64_t b = smem_desc_sw128(v0 + kk * 2048, kPfKvHalf, 1024);
           umma_f16(tO, a, b, idO, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done);
         umma_commit(&bars->kv_empty[i % kPfStages]);
         return true;
       };
+      if (!mbar_wait(&bars->q_full, 0)) {
+        set_error(p.err, kErrWaitTimeout);
+        ok = false;
+      }
       for (int j = 0; j < nkv && ok; ++j) {
         const int s = j % kPfStages;
         if (!mbar_wait(&bars->kv_full[s], (j / kPfStages) & 1) ||
@@ -209,7 +216,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t a = smem_desc_sw128(q0 + (kk >> 2) * kPfSwHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = smem_desc_sw128(k0 + (kk >> 2) * kPfSwHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = smem_desc_sw128(k0 + (kk >> 2) * kPfKvHalf + (kk & 3) * 32, 16, 1024);
           umma_f16(tS, a, b, idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full);
@@ -223,6 +230,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax (one row per thread)
+    {  // stage Q (zeros for rows past the tile's tokens) while the first K/V tiles load
+      const T* src = static_cast<const T*>(p.q) + int64_t(tokbase + t0 + t_eff) * p.q_st +
+                     int64_t(kvh * G + g_row) * p.q_sh;
+      uint4 qv[D / 8];
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c)
+        qv[c] = row_valid ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(sQ + (c >> 3) * kPfSwHalf + sw_off(r, c & 7)) = qv[c];
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->q_full);
+    }
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < nkv; ++j) {
@@ -235,8 +254,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       uint32_t sr[kPfKeys];
       tmem_ld32_at<0>(tS + lane_base + 0, sr);
       tmem_ld32_at<32>(tS + lane_base + 32, sr);
-      tmem_ld32_at<64>(tS + lane_base + 64, sr);
-      tmem_ld32_at<96>(tS + lane_base + 96, sr);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars->s_consumed);
@@ -254,7 +271,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int first = ctx - kbase;
         for (int c = tid; c < (kPfKeys - first) * NH * 8; c += 128) {
           const int row = first + c / (NH * 8), rest = c % (NH * 8);
-          *reinterpret_cast<uint4*>(vst + (rest >> 3) * kPfSwHalf + row * 128 + (rest & 7) * 16) =
+          *reinterpret_cast<uint4*>(vst + (rest >> 3) * kPfKvHalf + row * 128 + (rest & 7) * 16) =
               make_uint4(0, 0, 0, 0);
         }
       }
@@ -263,18 +280,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kPfKeys; ++c) {
-        const float v = c <= lim ? __uint_as_float(sr[c]) * p.qscale : -INFINITY;
+        const float v = c <= lim ? __uint_as_float(sr[c]) : -INFINITY;
         sr[c] = __float_as_uint(v);
         mx = fmaxf(mx, v);
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
+      // Scores are raw q.k here; the softmax scale (> 0) is folded into the exponent.  The
+      // subtracted maximum is only raised when the tile's maximum exceeds it by more than
+      // kLazyRescale (log2 units): softmax is unchanged by the choice of that constant as
+      // long as O and l share it, probabilities stay <= 2^kLazyRescale, and most tiles
+      // then skip the rescale of O in TMEM.
+      const float mx_s = mx * p.qscale;
+      const bool grow = mx_s > m_run + kLazyRescale;
+      const float m_new = grow ? mx_s : m_run;
+      const float alpha = grow ? ex2(m_run - m_new) : 1.f;
       float rs = 0.f;
       uint32_t pk[kPfKeys / 2];
 #pragma unroll
       for (int c = 0; c < kPfKeys; c += 2) {
-        const float e0 = exp2f(__uint_as_float(sr[c]) - m_new);
-        const float e1 = exp2f(__uint_as_float(sr[c + 1]) - m_new);
+        const float e0 = ex2(fmaf(__uint_as_float(sr[c]), p.qscale, -m_new));
+        const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), p.qscale, -m_new));
         rs += e0 + e1;
         pk[c / 2] = pack2<T>(e0, e1);
       }
@@ -291,17 +315,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < kPfKeys / 8; ++c)
-        *reinterpret_cast<uint4*>(sP + (c >> 3) * kPfSwHalf + sw_off(r, c & 7)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      if (j > 0) {
+        *reinterpret_cast<uint4*>(sP + sw_off(r, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_base + 32 * c, o);
+        for (int c = 0; c < D / 64; ++c) {  // 64 columns per TMEM round trip
+          uint32_t o[64];
+          tmem_ld32_at<0>(tO + lane_base + 64 * c, o);
+          tmem_ld32_at<32>(tO + lane_base + 64 * c + 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tO + lane_base + 32 * c, o);
+          for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + lane_base + 64 * c, *reinterpret_cast<const uint32_t(*)[32]>(&o[0]));
+          tmem_st32(tO + lane_base + 64 * c + 32, *reinterpret_cast<const uint32_t(*)[32]>(&o[32]));
         }
         tmem_wait_st();
       }
@@ -342,7 +367,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 5) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tbase, kPfTmemCols);
+    tmem_dealloc(tbase, C::TMEM_COLS);
   }
 }
 
