@@ -63,8 +63,8 @@ struct PfCfg {
 };
 
 struct PfBars {
-  uint64_t kv_full[kPfStages];
-  uint64_t kv_empty[kPfStages];
+  uint64_t k_full[kPfStages], k_empty[kPfStages];  // K ring: freed once S = Q.K^T retires
+  uint64_t v_full[kPfStages], v_empty[kPfStages];  // V ring: freed once O += P.V retires
   uint64_t q_full, s_full, s_consumed, p_ready, pv_done;
   uint32_t tmem_base;
 };
@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   }
   if (tid == 0) {
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->q_full, 128);
     mbar_init(&bars->s_full, 1);
@@ -155,28 +157,39 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       prefetch_tmap(&tv);
       for (int j = 0; j < nkv && ok; ++j) {
         const int s = j % kPfStages;
-        if (j >= kPfStages && !mbar_wait(&bars->kv_empty[s], ((j / kPfStages) - 1) & 1)) {
-          set_error(p.err, kErrWaitTimeout);
-          ok = false;
-          break;
-        }
         const int b0 = j * kPfBlocks;
         const int nload = min(kPfBlocks, nblk_seq - b0);
         uint8_t* kst = sST + s * C::STAGE;
         uint8_t* vst = kst + C::K_BYTES;
-        mbar_arrive_expect_tx(&bars->kv_full[s], uint32_t(nload * NH * 2 * 2048));
+        int phys[kPfBlocks];
         for (int b = 0; b < nload; ++b) {
-          int phys = trow[b0 + b];
-          if (phys < 0 || phys >= p.pool_blocks) {  // the host planner rejects these
+          phys[b] = trow[b0 + b];
+          if (phys[b] < 0 || phys[b] >= p.pool_blocks) {  // the host planner rejects these
             set_error(p.err, kErrBlockId);
-            phys = 0;
-          }
-#pragma unroll
-          for (int h = 0; h < NH; ++h) {
-            tma_load_3d(kst + h * kPfKvHalf + b * 2048, &tk, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
-            tma_load_3d(vst + h * kPfKvHalf + b * 2048, &tv, 64 * h, kvh, phys * 16, &bars->kv_full[s]);
+            phys[b] = 0;
           }
         }
+        const uint32_t bytes = uint32_t(nload * NH * 2048);
+        if (j >= kPfStages && !mbar_wait(&bars->k_empty[s], ((j / kPfStages) - 1) & 1)) {
+          set_error(p.err, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->k_full[s], bytes);
+        for (int b = 0; b < nload; ++b)
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+            tma_load_3d(kst + h * kPfKvHalf + b * 2048, &tk, 64 * h, kvh, phys[b] * 16, &bars->k_full[s]);
+        if (j >= kPfStages && !mbar_wait(&bars->v_empty[s], ((j / kPfStages) - 1) & 1)) {
+          set_error(p.err, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->v_full[s], bytes);
+        for (int b = 0; b < nload; ++b)
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+            tma_load_3d(vst + h * kPfKvHalf + b * 2048, &tv, 64 * h, kvh, phys[b] * 16, &bars->v_full[s]);
       }
     }
   } else if (warp == 5) {
@@ -186,7 +199,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       constexpr uint32_t idO = idesc_f16<T>(kPfRows, D, true);
       const uint32_t q0 = smem_u32(sQ), p0 = smem_u32(sP);
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(&bars->p_ready, i & 1)) return false;
+        if (!mbar_wait(&bars->p_ready, i & 1) || !mbar_wait(&bars->v_full[i % kPfStages], (i / kPfStages) & 1))
+          return false;
         tc_fence_after();
         const uint32_t v0 = smem_u32(sST + (i % kPfStages) * C::STAGE + C::K_BYTES);
 #pragma unroll
@@ -196,7 +210,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           umma_f16(tO, a, b, idO, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done);
-        umma_commit(&bars->kv_empty[i % kPfStages]);
+        umma_commit(&bars->v_empty[i % kPfStages]);
         return true;
       };
       if (!mbar_wait(&bars->q_full, 0)) {
@@ -205,7 +219,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       }
       for (int j = 0; j < nkv && ok; ++j) {
         const int s = j % kPfStages;
-        if (!mbar_wait(&bars->kv_full[s], (j / kPfStages) & 1) ||
+        if (!mbar_wait(&bars->k_full[s], (j / kPfStages) & 1) ||
             (j > 0 && !mbar_wait(&bars->s_consumed, (j - 1) & 1))) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
@@ -220,6 +234,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           umma_f16(tS, a, b, idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full);
+        umma_commit(&bars->k_empty[s]);
         if (j > 0 && !issue_pv(j - 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
@@ -262,7 +277,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const int kbase = j * kPfKeys;
       if (ctx - kbase < kPfKeys) {
         const int s = j % kPfStages;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_full[s], (j / kPfStages) & 1));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->v_full[s], (j / kPfStages) & 1));
         if (!ok) {
           if (lane == 0) set_error(p.err, kErrWaitTimeout);
           break;
