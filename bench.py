@@ -84,11 +84,11 @@ class Workload:
 
     def __init__(self, batch: int, layers: int, heads: int, kv_heads: int, head_dim: int, block_size: int,
                  mean_ctx: float, lo: int, hi: int, sigma: float, seed: int, max_steps: int, churn: float,
-                 prompt_lo: int = 256, prompt_hi: int = 2048):
+                 prompt_lo: int = 256, prompt_hi: int = 2048, median_ctx: float | None = None):
         self.batch, self.layers, self.heads, self.kv_heads = batch, layers, heads, kv_heads
         self.head_dim, self.block_size = head_dim, block_size
         rng = np.random.default_rng(seed)
-        mu = clipped_lognormal_mu(mean_ctx, sigma, lo, hi)
+        mu = np.log(median_ctx) if median_ctx else clipped_lognormal_mu(mean_ctx, sigma, lo, hi)
         self.ctx0 = np.clip(np.exp(rng.normal(mu, sigma, size=batch)), lo, hi).astype(np.int64)
         need = -(-(self.ctx0 + max_steps) // block_size)
         self.n_churn = int(round(churn * batch))
@@ -240,27 +240,28 @@ def _blas_threads() -> int:
         return 1
 
 
-def _oracle_layer_timer(wl: Workload, nseq: int):
+def _oracle_layer_timer(wl: Workload, nseq: int, dtype: str = "bf16"):
     """One layer of the oracle's decode step (KV append + gather-path attention) on a
     sample of `nseq` sequences; returns a function that runs it and returns seconds."""
     from oracle import paged_attention_oracle as oracle
 
-    q, kp, vp, tables, ctx, ql, knew, vnew, slots = _sample_for_cpu(wl, nseq, 0, "bf16", seed=1234)
+    q, kp, vp, tables, ctx, ql, knew, vnew, slots = _sample_for_cpu(wl, nseq, 0, dtype, seed=1234)
     scale = wl.head_dim ** -0.5
 
     def one():
         t0 = time.perf_counter()
         kp2 = oracle.kv_append(kp, slots, knew)
         vp2 = oracle.kv_append(vp, slots, vnew)
-        oracle.paged_attention_gather(q, kp2, vp2, tables, ctx, ql, scale, "bf16")
+        oracle.paged_attention_gather(q, kp2, vp2, tables, ctx, ql, scale, dtype)
         return time.perf_counter() - t0
 
     return one, ctx
 
 
-def _cpu_sample_text(wl: Workload, nseq: int, ctx, reps: int) -> str:
+def _cpu_sample_text(wl: Workload, nseq: int, ctx, reps: int, dtype: str = "bf16") -> str:
+    how = "bf16 emulated in float32 numpy" if dtype == "bf16" else "float32 numpy"
     return (f"{nseq} decode sequences of the workload (contexts {ctx.tolist()}), {reps} repetitions of one layer "
-            f"of the oracle's KV append + gather-path attention (bf16 emulated in float32 numpy), scaled to "
+            f"of the oracle's KV append + gather-path attention ({how}), scaled to "
             f"{wl.layers} layers and to decode tokens/s; churn prefill not included; host has "
             f"{os.cpu_count()} CPUs")
 
@@ -271,7 +272,8 @@ def run_reference(args, rank: int, world: int) -> None:
         return
     wl = _make_workload(args, rank, max_steps=1)
     nseq = args.cpu_sample_seqs
-    one, ctx = _oracle_layer_timer(wl, nseq)
+    dt = WORKLOADS[args.workload]["dtype"]
+    one, ctx = _oracle_layer_timer(wl, nseq, dt)
     for _ in range(args.warmup):
         one()
     times = [one() for _ in range(args.steps)]
@@ -280,10 +282,10 @@ def run_reference(args, rank: int, world: int) -> None:
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_layer * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic",
         "config": _config(args, wl, world),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": _blas_threads(), "kind": "port",
-                         "sample": _cpu_sample_text(wl, nseq, ctx, len(times))},
+                         "sample": _cpu_sample_text(wl, nseq, ctx, len(times), dt)},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "host_cpus": os.cpu_count(),
     }
@@ -291,18 +293,40 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ------------------------------------------------------------------ GPU arm
+WORKLOADS = {
+    # BASELINE config 3 (the default line): Llama-3-8B shape with churn prefill.
+    "config3": dict(heads=32, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=4096.0, median_ctx=None,
+                    lo=128, hi=16384, layers=32, churn=0.05),
+    # the isolated paged-decode microbenchmark, GPT-2 heads.
+    "config2-f32": dict(heads=12, kv_heads=12, head_dim=64, dtype="f32", mean_ctx=0.0, median_ctx=1024.0,
+                        lo=16, hi=8192, layers=1, churn=0.0),
+    "config2-bf16": dict(heads=12, kv_heads=12, head_dim=64, dtype="bf16", mean_ctx=0.0, median_ctx=1024.0,
+                         lo=16, hi=8192, layers=1, churn=0.0),
+}
+
+
 def _make_workload(args, rank: int, max_steps: int) -> Workload:
-    return Workload(batch=args.batch, layers=args.layers, heads=32, kv_heads=8, head_dim=128, block_size=16,
-                    mean_ctx=4096.0, lo=128, hi=16384, sigma=0.9, seed=args.seed + rank, max_steps=max_steps,
-                    churn=args.churn)
+    w = WORKLOADS[args.workload]
+    return Workload(batch=args.batch, layers=args.layers, heads=w["heads"], kv_heads=w["kv_heads"],
+                    head_dim=w["head_dim"], block_size=16, mean_ctx=w["mean_ctx"], lo=w["lo"], hi=w["hi"],
+                    sigma=0.9, seed=args.seed + rank, max_steps=max_steps, churn=args.churn,
+                    median_ctx=w["median_ctx"])
 
 
 def _config(args, wl: Workload, world: int) -> dict:
+    if args.workload == "config3":
+        desc = ("BASELINE config 3: Llama-3-8B-shape GQA paged attention (32 q / 8 kv heads, head_dim 128, "
+                "bf16, 32 layers, block 16), batch 256, contexts lognormal mean 4096 clipped 128..16384, "
+                f"{wl.n_churn} churn prompts of 256..2048 tokens per step through varlen paged prefill")
+        model = "llama3-8b-shape attention hot path (random-init)"
+    else:
+        desc = (f"BASELINE config 2: isolated paged-decode attention microbenchmark, GPT-2 shape (12 heads, "
+                f"head_dim 64, {WORKLOADS[args.workload]['dtype']}, block 16), batch 256, contexts lognormal "
+                f"median 1024 clipped 16..8192, {wl.layers} layer(s) per step")
+        model = "gpt2-shape attention (random-init)"
     return {
-        "workload": "BASELINE config 3: Llama-3-8B-shape GQA paged attention (32 q / 8 kv heads, head_dim 128, "
-                    "bf16, 32 layers, block 16), batch 256, contexts lognormal mean 4096 clipped 128..16384, "
-                    f"{wl.n_churn} churn prompts of 256..2048 tokens per step through varlen paged prefill",
-        "model": "llama3-8b-shape attention hot path (random-init)",
+        "workload": desc,
+        "model": model,
         "global_batch": wl.batch * world,
         "batch_per_gpu": wl.batch,
         "churn_prompts_per_step": wl.n_churn,
@@ -310,7 +334,7 @@ def _config(args, wl: Workload, world: int) -> dict:
         "heads": wl.heads, "kv_heads": wl.kv_heads, "head_dim": wl.head_dim, "block_size": wl.block_size,
         "sum_context_step0": int(wl.ctx0.sum()),
         "seq_len": "ragged (mean 4096)",
-        "l2": "inputs larger than L2 (each layer's KV is ~4.3 GB vs 126 MB L2); no flush",
+        "l2": f"inputs larger than L2 (each layer's KV is {wl.attention_bytes(0, 2 if args.workload != 'config2-f32' else 4) / 1e9:.2f} GB vs 126 MB L2); no flush",
         "parallelism": f"replicas x{world} (request-level data parallel, no collectives)",
         "step": "prefill pass for the churn prompts + decode pass for the batch; per layer: fused K+V append, "
                 "then paged attention",
@@ -336,7 +360,8 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     steps_total = args.warmup + args.steps
     wl = _make_workload(args, rank, max_steps=steps_total + 1)
     L, B, Hq, Hkv, D, BS = wl.layers, wl.batch, wl.heads, wl.kv_heads, wl.head_dim, wl.block_size
-    dtype, elem = torch.bfloat16, 2
+    f32 = WORKLOADS[args.workload]["dtype"] == "f32"
+    dtype, elem = (torch.float32, 4) if f32 else (torch.bfloat16, 2)
     tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
     sm = pkg.metadata.sm_count(dev)
 
@@ -486,12 +511,13 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     bytes_per_call = float(np.mean([wl.attention_bytes(s, elem) for s in timed]))
     achieved = bytes_per_call / (dec_avg_ms / 1e3) / 1e9
     hbm_peak, bf16_peak, peak_kind = _measured_peaks()
-    traffic = _traffic_per_call(float(np.mean([wl.context_lens(s).sum() for s in timed])))
+    traffic = (_traffic_per_call(float(np.mean([wl.context_lens(s).sum() for s in timed])))
+               if args.workload == "config3" else None)
     pre_flops = float(np.mean([wl.prefill_flops(s) for s in timed])) if wl.n_churn else 0.0
     pre_tflops = pre_flops / (pre_avg_ms / 1e3) / 1e12 if wl.n_churn else None
 
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.workload == "config3":
         one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs)
         one()
         t_end = time.perf_counter() + args.cpu_budget_s
@@ -505,12 +531,13 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if f32 else "bf16", "data": "synthetic",
         "config": _config(args, wl, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy ({source} hbm_gbs)",
                      "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS, "traffic": traffic,
-                     "kernel": "decode paged attention per layer (tensor-pipe split-K decode + combine)",
+                     "kernel": "decode paged attention per layer (split-K decode + combine; "
+                               + ("SIMT fp32" if f32 else "tensor-pipe MMA") + ")",
                      "algorithmic_bytes_per_launch": bytes_per_call, "avg_launch_ms": dec_avg_ms},
         "prefill_roofline": None if not wl.n_churn else {
             "bound": "tensor", "achieved": pre_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
@@ -551,13 +578,20 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--batch", type=int, default=256)
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--churn", type=float, default=0.05, help="fraction of the batch re-admitted per step")
+    ap.add_argument("--layers", type=int, default=None, help="default: the workload's (32 for config3)")
+    ap.add_argument("--churn", type=float, default=None,
+                    help="fraction of the batch re-admitted per step (default: the workload's, 0.05 for config3)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
+                    help="config3 (default headline) or BASELINE config 2's isolated decode microbenchmark")
     ap.add_argument("--cpu-sample-seqs", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.layers is None:
+        args.layers = WORKLOADS[args.workload]["layers"]
+    if args.churn is None:
+        args.churn = WORKLOADS[args.workload]["churn"]
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
