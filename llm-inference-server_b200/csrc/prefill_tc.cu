@@ -292,13 +292,15 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       }
 
       const int lim = qpos - kbase;  // key column c is visible iff c <= lim
-      float mx = -INFINITY;
+      // Four independent max / sum chains instead of one 64-long dependency chain.
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < kPfKeys; ++c) {
         const float v = c <= lim ? __uint_as_float(sr[c]) : -INFINITY;
         sr[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        mx4[c & 3] = fmaxf(mx4[c & 3], v);
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       // Scores are raw q.k here; the softmax scale (> 0) is folded into the exponent.  The
       // subtracted maximum is only raised when the tile's maximum exceeds it by more than
       // kLazyRescale (log2 units): softmax is unchanged by the choice of that constant as
@@ -308,15 +310,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const bool grow = mx_s > m_run + kLazyRescale;
       const float m_new = grow ? mx_s : m_run;
       const float alpha = grow ? ex2(m_run - m_new) : 1.f;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kPfKeys / 2];
 #pragma unroll
       for (int c = 0; c < kPfKeys; c += 2) {
         const float e0 = ex2(fmaf(__uint_as_float(sr[c]), p.qscale, -m_new));
         const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), p.qscale, -m_new));
-        rs += e0 + e1;
+        rs4[(c >> 1) & 3] += e0 + e1;
         pk[c / 2] = pack2<T>(e0, e1);
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l_run = l_run * alpha + rs;
       m_run = m_new;
 
