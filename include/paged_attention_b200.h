@@ -71,7 +71,7 @@ typedef struct pa_step_plan {
   int64_t off_slot_mapping;    /* [T] flat pool slot each new token's K/V is written to */
   int64_t off_decode_items;    /* [num_decode_items][4] seq, split, part, nsplit */
   int64_t off_combine;         /* [num_combine_seqs][4] seq, token, first part, nsplit */
-  int64_t off_prefill_tiles;   /* [num_prefill_tiles][2] seq, first query row */
+  int64_t off_prefill_tiles;   /* [num_prefill_tiles][2] seq, first query row; most keys first */
   int64_t words;               /* int32 words used in the packed buffer */
 } pa_step_plan;
 

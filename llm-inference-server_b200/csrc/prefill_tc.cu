@@ -9,18 +9,22 @@
 // tokens of one sequence; its 128 rows are the (token, query head) pairs of those tokens
 // and the G = Hq / Hkv query heads sharing the KV head (row r = token r / G, head r % G),
 // so every K/V byte a CTA loads serves all G heads.  KV is walked in tiles of 64 keys
-// (4 pool blocks) up to the causal limit of the tile's last token.  The footprint
-// (112 KB of shared memory and 256 TMEM columns at head_dim 128) lets two CTAs share an
-// SM, so one CTA's softmax and latencies overlap the other's MMAs.
+// (4 pool blocks) up to the causal limit of the tile's last token.  Q lives in TMEM (the
+// A operand of S = Q.K^T comes straight from tensor memory), so shared memory holds only
+// P and 3-deep K and V rings: 112 KB of shared memory and 256 TMEM columns at head_dim
+// 128 let two CTAs share an SM, so one CTA's softmax and latencies overlap the other's
+// MMAs.
 //
 // Roles (192 threads):
-//   warps 0-3  one thread per row: stage Q (overlapping the first K/V loads), softmax,
-//              O rescale, epilogue.  Row r lives in TMEM lane r, so row max and row sum
+//   warps 0-3  one thread per row: write Q into TMEM (overlapping the first K/V loads),
+//              softmax, O rescale, epilogue.  Row r lives in TMEM lane r, so row max and row sum
 //              are thread-local.
 //   warp 4     TMA producer: per KV tile, 4 blocks x (head_dim/64) boxes of K and of V
-//              (128-byte swizzle) into a 2-stage ring; block ids come from the table.
-//   warp 5     allocates TMEM (S: 64 columns, O: head_dim columns) and issues MMAs:
-//              S = Q.K^T (M=128, N=64, K=16 per instruction; Q and K K-major) and
+//              (128-byte swizzle) into 3-stage rings; block ids come from the table.
+//   warp 5     allocates TMEM (S: 64 columns, O: head_dim columns, Q: head_dim / 2
+//              columns of packed pairs) and issues MMAs:
+//              S = Q.K^T (M=128, N=64, K=16 per instruction; Q K-major from TMEM, K
+//              K-major from shared memory) and
 //              O += P.V (M=128, N=head_dim; P K-major from shared memory, V MN-major).
 // Per KV tile j: TMA(K_j,V_j) -> MMA S_j -> softmax j reads S (s_consumed) while MMA
 // may already start S_{j+1} -> softmax waits PV_{j-1}, writes P_j (bf16/fp16, swizzled)
@@ -41,7 +45,7 @@ namespace pa {
 constexpr int kPfRows = 128;
 constexpr int kPfKeys = 64;
 constexpr int kPfBlocks = kPfKeys / 16;
-constexpr int kPfStages = 2;
+constexpr int kPfStages = 3;
 constexpr int kPfThreads = 192;
 constexpr int kPfSwHalf = kPfRows * 128;  // one 64-element-wide swizzled column half of a 128-row tile
 constexpr int kPfKvHalf = kPfKeys * 128;  // the same for a 64-key K or V tile
@@ -50,16 +54,15 @@ constexpr float kLazyRescale = 8.f;        // raise the running row max only pas
 template <int D>
 struct PfCfg {
   static constexpr int NH = D / 64;
-  static constexpr int Q_BYTES = NH * kPfSwHalf;
   static constexpr int P_BYTES = kPfSwHalf;          // 128 rows x 64 keys
   static constexpr int K_BYTES = NH * kPfKvHalf;
-  static constexpr int STAGE = 2 * K_BYTES;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_P = OFF_Q + Q_BYTES;
+  static constexpr int STAGE = 2 * K_BYTES;          // K tile then V tile
+  static constexpr int OFF_P = 0;
   static constexpr int OFF_ST = OFF_P + P_BYTES;
   static constexpr int OFF_BAR = OFF_ST + kPfStages * STAGE;
-  static constexpr int SMEM = OFF_BAR + 128;
-  static constexpr uint32_t TMEM_COLS = (kPfKeys + D) <= 128 ? 128u : 256u;  // S then O
+  static constexpr int SMEM = OFF_BAR + 256;
+  static constexpr uint32_t TMEM_COLS = 256;         // S (64), O (D), Q (D / 2)
+  static_assert(kPfKeys + D + D / 2 <= 256, "TMEM budget");
 };
 
 struct PfBars {
@@ -102,10 +105,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   constexpr int NH = C::NH;
   constexpr int TQ = kPfRows / G;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sP = smem + C::OFF_P;
   uint8_t* sST = smem + C::OFF_ST;
   PfBars* bars = reinterpret_cast<PfBars*>(smem + C::OFF_BAR);
+  static_assert(sizeof(PfBars) <= 256, "barrier area");
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int2 tile = p.tiles[blockIdx.x];
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
-  const uint32_t tS = tbase, tO = tbase + kPfKeys;
+  const uint32_t tS = tbase, tO = tbase + kPfKeys, tQ = tbase + kPfKeys + D;
   bool ok = true;
 
   // Row of this thread (softmax warps): token t = r / G, query head kvh*G + r % G.
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_f16<T>(kPfRows, kPfKeys, false);
       constexpr uint32_t idO = idesc_f16<T>(kPfRows, D, true);
-      const uint32_t q0 = smem_u32(sQ), p0 = smem_u32(sP);
+      const uint32_t p0 = smem_u32(sP);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(&bars->p_ready, i & 1) || !mbar_wait(&bars->v_full[i % kPfStages], (i / kPfStages) & 1))
           return false;
@@ -229,9 +232,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         const uint32_t k0 = smem_u32(sST + s * C::STAGE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = smem_desc_sw128(q0 + (kk >> 2) * kPfSwHalf + (kk & 3) * 32, 16, 1024);
           const uint64_t b = smem_desc_sw128(k0 + (kk >> 2) * kPfKvHalf + (kk & 3) * 32, 16, 1024);
-          umma_f16(tS, a, b, idS, kk > 0 ? 1u : 0u);
+          umma_f16_ts(tS, tQ + 8 * kk, b, idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full);
         umma_commit(&bars->k_empty[s]);
@@ -245,19 +247,26 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     }
   } else {
     // ------------------------------------------------------------ softmax (one row per thread)
-    {  // stage Q (zeros for rows past the tile's tokens) while the first K/V tiles load
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    {  // Q row -> TMEM lane r (zeros for rows past the tile's tokens) while K/V tiles load
       const T* src = static_cast<const T*>(p.q) + int64_t(tokbase + t0 + t_eff) * p.q_st +
                      int64_t(kvh * G + g_row) * p.q_sh;
-      uint4 qv[D / 8];
+      uint32_t qw[D / 2];
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c)
-        qv[c] = row_valid ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 v = row_valid ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
+        qw[4 * c + 0] = v.x;
+        qw[4 * c + 1] = v.y;
+        qw[4 * c + 2] = v.z;
+        qw[4 * c + 3] = v.w;
+      }
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(sQ + (c >> 3) * kPfSwHalf + sw_off(r, c & 7)) = qv[c];
-      fence_proxy_async_smem();
+      for (int c = 0; c < D / 64; ++c)
+        tmem_st32(tQ + lane_base + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(&qw[32 * c]));
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(&bars->q_full);
     }
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < nkv; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full, j & 1));  // reconverge before .sync.aligned
@@ -294,11 +303,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const int lim = qpos - kbase;  // key column c is visible iff c <= lim
       // Four independent max / sum chains instead of one 64-long dependency chain.
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__any_sync(0xffffffffu, lim < kPfKeys - 1)) {  // the tile crosses the causal diagonal
 #pragma unroll
-      for (int c = 0; c < kPfKeys; ++c) {
-        const float v = c <= lim ? __uint_as_float(sr[c]) : -INFINITY;
-        sr[c] = __float_as_uint(v);
-        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+        for (int c = 0; c < kPfKeys; ++c) {
+          const float v = c <= lim ? __uint_as_float(sr[c]) : -INFINITY;
+          sr[c] = __float_as_uint(v);
+          mx4[c & 3] = fmaxf(mx4[c & 3], v);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kPfKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
       }
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       // Scores are raw q.k here; the softmax scale (> 0) is folded into the exponent.  The

@@ -244,16 +244,25 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
       ++w;
     }
 
+  // Prefill tiles in launch order, heaviest first: a tile's work is the causal key range
+  // of its last token, so the grid's tail is made of the tiles with the fewest keys
+  // (longest-processing-time-first list scheduling over the SMs).
   if (n_tiles > 0) {
     int32_t* tiles = meta_out + plan->off_prefill_tiles;
-    int64_t k = 0;
+    struct Tile { int seq, row; int64_t keys; };
+    std::vector<Tile> list;
+    list.reserve(size_t(n_tiles));
     for (int i = 0; i < num_seqs; ++i)
       if (query_lens[i] > 1)
         for (int64_t r = 0; r < query_lens[i]; r += prefill_tile_tokens) {
-          tiles[2 * k + 0] = i;
-          tiles[2 * k + 1] = int32_t(r);
-          ++k;
+          const int64_t last = std::min<int64_t>(r + prefill_tile_tokens, query_lens[i]);
+          list.push_back({i, int32_t(r), context_lens[i] - query_lens[i] + last});
         }
+    std::stable_sort(list.begin(), list.end(), [](const Tile& a, const Tile& b) { return a.keys > b.keys; });
+    for (size_t k = 0; k < list.size(); ++k) {
+      tiles[2 * k + 0] = list[k].seq;
+      tiles[2 * k + 1] = list[k].row;
+    }
   }
   return PA_OK;
 }
