@@ -20,7 +20,9 @@
 //              softmax, O rescale, epilogue.  Row r lives in TMEM lane r, so row max and row sum
 //              are thread-local.
 //   warp 4     TMA producer: per KV tile, 4 blocks x (head_dim/64) boxes of K and of V
-//              (128-byte swizzle) into 3-stage rings; block ids come from the table.
+//              (128-byte swizzle) into 3-stage rings, one box per lane so a single warp
+//              instruction issues a tile's copies; block ids come from the table, read 8
+//              tiles at a time one group ahead of use.
 //   warp 5     allocates TMEM (S: 64 columns, O: head_dim columns, Q: head_dim / 2
 //              columns of packed pairs) and issues MMAs:
 //              S = Q.K^T (M=128, N=64, K=16 per instruction; Q K-major from TMEM, K
@@ -121,6 +123,36 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const int nblk_seq = (ctx + 15) / 16;
   const int32_t* trow = p.tables + int64_t(seq) * p.width;
 
+  // Row of this thread (softmax warps): token t = r / G, query head kvh*G + r % G.
+  const int r = tid;
+  const int t_row = r / G, g_row = r % G;
+  const bool row_valid = tid < kPfRows && t_row < ntok;
+  const int t_eff = min(t_row, ntok - 1);
+  const int qpos = ctx - ql + t0 + t_eff;
+
+  // Softmax threads start their Q row loads before the setup barrier.  Rows past the
+  // tile's tokens repeat its last token (finite scores; their outputs are never stored).
+  uint32_t qw[D / 2];
+  if (warp < 4) {
+    const T* src = static_cast<const T*>(p.q) + int64_t(tokbase + t0 + t_eff) * p.q_st +
+                   int64_t(kvh * G + g_row) * p.q_sh;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(src + 8 * c);
+      qw[4 * c + 0] = v.x;
+      qw[4 * c + 1] = v.y;
+      qw[4 * c + 2] = v.z;
+      qw[4 * c + 3] = v.w;
+    }
+  }
+  // Producer warp: block ids of 8 KV tiles (32 blocks) per coalesced warp load, each group
+  // read one group ahead of use.
+  int ids_cur = 0, ids_nxt = 0;
+  if (warp == 4) {
+    ids_cur = lane < nblk_seq ? trow[lane] : 0;
+    ids_nxt = 32 + lane < nblk_seq ? trow[32 + lane] : 0;
+  }
+
   if (warp == 5) {
     tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
@@ -146,55 +178,46 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const uint32_t tS = tbase, tO = tbase + kPfKeys, tQ = tbase + kPfKeys + D;
   bool ok = true;
 
-  // Row of this thread (softmax warps): token t = r / G, query head kvh*G + r % G.
-  const int r = tid;
-  const int t_row = r / G, g_row = r % G;
-  const bool row_valid = tid < kPfRows && t_row < ntok;
-  const int t_eff = min(t_row, ntok - 1);
-  const int qpos = ctx - ql + t0 + t_eff;
-
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
+    // The whole warp walks the tiles.  Lane l < 4 * (head_dim / 64) owns box l of each K
+    // and V tile (pool block l / NH, 64-column half l % NH), so one warp instruction issues
+    // all of a tile's copies; block ids are shuffled out of the group registers.
     if (lane == 0) {
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % kPfStages;
-        const int b0 = j * kPfBlocks;
-        const int nload = min(kPfBlocks, nblk_seq - b0);
-        uint8_t* kst = sST + s * C::STAGE;
-        uint8_t* vst = kst + C::K_BYTES;
-        int phys[kPfBlocks];
-        for (int b = 0; b < nload; ++b) {
-          phys[b] = trow[b0 + b];
-          if (phys[b] < 0 || phys[b] >= p.pool_blocks) {  // the host planner rejects these
-            set_error(p.err, kErrBlockId);
-            phys[b] = 0;
-          }
-        }
-        const uint32_t bytes = uint32_t(nload * NH * 2048);
-        if (j >= kPfStages && !mbar_wait(&bars->k_empty[s], ((j / kPfStages) - 1) & 1)) {
-          set_error(p.err, kErrWaitTimeout);
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&bars->k_full[s], bytes);
-        for (int b = 0; b < nload; ++b)
-#pragma unroll
-          for (int h = 0; h < NH; ++h)
-            tma_load_3d(kst + h * kPfKvHalf + b * 2048, &tk, 64 * h, kvh, phys[b] * 16, &bars->k_full[s]);
-        if (j >= kPfStages && !mbar_wait(&bars->v_empty[s], ((j / kPfStages) - 1) & 1)) {
-          set_error(p.err, kErrWaitTimeout);
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&bars->v_full[s], bytes);
-        for (int b = 0; b < nload; ++b)
-#pragma unroll
-          for (int h = 0; h < NH; ++h)
-            tma_load_3d(vst + h * kPfKvHalf + b * 2048, &tv, 64 * h, kvh, phys[b] * 16, &bars->v_full[s]);
-      }
     }
+    const int my_b = lane / NH, my_h = lane % NH;
+    bool pok = true;
+    for (int j = 0; j < nkv && pok; ++j) {
+      const int s = j % kPfStages;
+      const int b0 = j * kPfBlocks;
+      const int nload = min(kPfBlocks, nblk_seq - b0);
+      uint8_t* kst = sST + s * C::STAGE;
+      uint8_t* vst = kst + C::K_BYTES;
+      if (j > 0 && (j & 7) == 0) {
+        ids_cur = ids_nxt;
+        ids_nxt = b0 + 32 + lane < nblk_seq ? trow[b0 + 32 + lane] : 0;
+      }
+      const bool mine = lane < nload * NH;
+      int phys = __shfl_sync(0xffffffffu, ids_cur, (j & 7) * kPfBlocks + (my_b & (kPfBlocks - 1)));
+      if (mine && (phys < 0 || phys >= p.pool_blocks)) {  // the host planner rejects these
+        set_error(p.err, kErrBlockId);
+        phys = 0;
+      }
+      const uint32_t bytes = uint32_t(nload * NH * 2048);
+      if (j >= kPfStages) pok = __all_sync(0xffffffffu, mbar_wait(&bars->k_empty[s], ((j / kPfStages) - 1) & 1));
+      if (!pok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bars->k_full[s], bytes);
+      __syncwarp();
+      if (mine) tma_load_3d(kst + my_h * kPfKvHalf + my_b * 2048, &tk, 64 * my_h, kvh, phys * 16, &bars->k_full[s]);
+      if (j >= kPfStages) pok = __all_sync(0xffffffffu, mbar_wait(&bars->v_empty[s], ((j / kPfStages) - 1) & 1));
+      if (!pok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bars->v_full[s], bytes);
+      __syncwarp();
+      if (mine) tma_load_3d(vst + my_h * kPfKvHalf + my_b * 2048, &tv, 64 * my_h, kvh, phys * 16, &bars->v_full[s]);
+    }
+    if (!pok && lane == 0) set_error(p.err, kErrWaitTimeout);
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -248,18 +271,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   } else {
     // ------------------------------------------------------------ softmax (one row per thread)
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
-    {  // Q row -> TMEM lane r (zeros for rows past the tile's tokens) while K/V tiles load
-      const T* src = static_cast<const T*>(p.q) + int64_t(tokbase + t0 + t_eff) * p.q_st +
-                     int64_t(kvh * G + g_row) * p.q_sh;
-      uint32_t qw[D / 2];
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        const uint4 v = row_valid ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
-        qw[4 * c + 0] = v.x;
-        qw[4 * c + 1] = v.y;
-        qw[4 * c + 2] = v.z;
-        qw[4 * c + 3] = v.w;
-      }
+    {  // Q row -> TMEM lane r while the first K/V tiles load
 #pragma unroll
       for (int c = 0; c < D / 64; ++c)
         tmem_st32(tQ + lane_base + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(&qw[32 * c]));
@@ -373,19 +385,20 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const float inv = 1.f / l_run;
       T* dst = static_cast<T*>(p.out) + int64_t(tokbase + t0 + t_eff) * p.o_st + int64_t(kvh * G + g_row) * p.o_sh;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + lane_base + 32 * c, o);
+      for (int c = 0; c < D / 64; ++c) {  // 64 columns per TMEM round trip
+        uint32_t o[64];
+        tmem_ld32_at<0>(tO + lane_base + 64 * c, o);
+        tmem_ld32_at<32>(tO + lane_base + 64 * c + 32, o);
         tmem_wait_ld();
         if (row_valid) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
+          for (int e = 0; e < 64; e += 8) {
             uint4 w;
             w.x = pack2<T>(__uint_as_float(o[e + 0]) * inv, __uint_as_float(o[e + 1]) * inv);
             w.y = pack2<T>(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
             w.z = pack2<T>(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
             w.w = pack2<T>(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + 32 * c + e) = w;
+            *reinterpret_cast<uint4*>(dst + 64 * c + e) = w;
           }
         }
       }
