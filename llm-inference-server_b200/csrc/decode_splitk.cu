@@ -92,9 +92,11 @@ __global__ void __launch_bounds__(32 * kDecodeWarps)
   float* pbuf_all = reinterpret_cast<float*>(smem + C::TILES_BYTES + C::BAR_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int4 item = p.items[blockIdx.x];
+  // KV head fastest: the heads of one work item run side by side, so the row slices of
+  // each pool block they read reach DRAM close together.
+  const int4 item = p.items[blockIdx.x / p.num_kv_heads];
   const int seq = item.x, split = item.y, part = item.z, nsplit = item.w;
-  const int kvh = blockIdx.y;
+  const int kvh = blockIdx.x % p.num_kv_heads;
   const int ctx = p.ctx_lens[seq];
   const int tok = p.cu_q[seq];
   const int b0 = split * p.split_blocks;
@@ -331,7 +333,7 @@ static cudaError_t launch_one(const CUtensorMap& tk, const CUtensorMap& tv, cons
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(p.num_items, p.num_kv_heads), block(32 * kDecodeWarps);
+  dim3 grid(p.num_items * p.num_kv_heads), block(32 * kDecodeWarps);
   kern<<<grid, block, C::SMEM, stream>>>(tk, tv, p);
   return cudaGetLastError();
 }
