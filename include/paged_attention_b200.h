@@ -6,6 +6,8 @@
  *                                                block_tables, context_lens, query_lens, scale)
  *   inference_server/core/paged_executor.py:116-125  _PagedCache.update (KV append)
  *   inference_server/core/paged_executor.py:211-263  _pack (per-step ragged metadata)
+ *   inference_server/core/kv_pool.py:142-182 and paged_executor.py:265-270  block swap
+ *                                                and copy-on-write moves
  *
  * Plain C types only: device pointers, element strides, sizes and a dtype enum.  The
  * library owns no device memory: the caller allocates outputs, the packed metadata
@@ -194,6 +196,41 @@ int32_t pa_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_
                              int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
                              int32_t dtype, void* k_pool, void* v_pool, int64_t pool_num_blocks,
                              int32_t block_size, const int32_t* slot_mapping, void* stream);
+
+/*
+ * Whole-block moves across every layer's K and V pools, one launch per 128 layers.
+ * The pools are the reference layout; block_bytes = block_size * num_kv_heads * head_dim
+ * * element size (a multiple of 16; pools and staging 16-byte aligned).  k_pools and
+ * v_pools are HOST arrays of num_layers device pointers.  Block ids are device int32;
+ * an id outside [0, pool_num_blocks) sets bit 1 of *error_word (device int32, required)
+ * and that block is skipped.  The moves are bitwise and asynchronous on `stream`.
+ *
+ * pa_copy_blocks: pool[dst] = pool[src] in every layer, for pairs [num_pairs][2]
+ * (src, dst).  Replaces inference_server/core/paged_executor.py:265-270 (_copy_block,
+ * the copy-on-write move BlockTable.ensure_private asks for, one block and one layer at
+ * a time).  Precondition: the destinations are distinct and none is also a source (the
+ * pairs run concurrently).
+ */
+int32_t pa_copy_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                       int64_t block_bytes, const int32_t* pairs, int32_t num_pairs, int32_t* error_word,
+                       void* stream);
+
+/*
+ * pa_gather_blocks: copy blocks[0..num_blocks) of every layer into `staging`, laid out
+ * [num_layers][K, V][num_blocks][block_bytes] — each [layer][K or V] slice is the
+ * reference's per-layer host tensor [num_blocks, block_size, Hkv, D].  Replaces the
+ * per-layer index_select of inference_server/core/kv_pool.py:142-166 (swap_out); the
+ * caller then moves staging to host memory with one copy.
+ *
+ * pa_scatter_blocks: the inverse, staging -> blocks (inference_server/core/kv_pool.py:
+ * 168-182, swap_in's per-layer index_copy_).  Precondition: the blocks are distinct.
+ */
+int32_t pa_gather_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                         int64_t block_bytes, const int32_t* blocks, int32_t num_blocks, void* staging,
+                         int32_t* error_word, void* stream);
+int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                          int64_t block_bytes, const int32_t* blocks, int32_t num_blocks, const void* staging,
+                          int32_t* error_word, void* stream);
 
 /*
  * Read (and clear, when clear != 0) the device error word a workspace carries.  It is

@@ -19,7 +19,7 @@ The directory name is not a Python identifier; the package is imported under the
 from __future__ import annotations
 
 from .attention import paged_attention, paged_attention_cuda, read_device_error
-from .kv_cache import KVPool, allocate_pool, reshape_and_cache
+from .kv_cache import HostBlocks, KVPool, allocate_pool, copy_blocks, reshape_and_cache
 from .metadata import StepMetadata, attach, attached
 
 __all__ = [
@@ -29,6 +29,8 @@ __all__ = [
     "reshape_and_cache",
     "allocate_pool",
     "KVPool",
+    "HostBlocks",
+    "copy_blocks",
     "StepMetadata",
     "attach",
     "attached",

@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class StepPlan(ctypes.Structure):
@@ -94,6 +94,12 @@ _SIGNATURES = {
                                                  c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_float,
                                                  POINTER(StepPlan), c_void_p, c_void_p, c_int64, c_int64,
                                                  c_void_p]),
+    "pa_copy_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p, c_int32,
+                                 c_void_p, c_void_p]),
+    "pa_gather_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p,
+                                   c_int32, c_void_p, c_void_p, c_void_p]),
+    "pa_scatter_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p,
+                                    c_int32, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

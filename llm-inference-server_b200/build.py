@@ -26,7 +26,8 @@ LIB_NAME = "libpaged_attn_b200.so"
 LIB = PKG / LIB_NAME
 
 CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "prefill_tc.cu", "attention_generic.cu", "kv_append.cu",
-              "attention_noalloc.cu"]
+              "attention_noalloc.cu",
+              "block_copy.cu"]
 CXX_SOURCES = ["step_plan.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

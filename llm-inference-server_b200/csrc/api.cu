@@ -2,6 +2,7 @@
 // TMA descriptor encoding (cached per pool), workspace layout and kernel dispatch.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -324,6 +325,64 @@ int32_t pa_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_
   cudaError_t e = launch_append(p, static_cast<cudaStream_t>(stream_ptr));
   if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache launch");
   return PA_OK;
+}
+
+static int32_t block_move(int32_t mode, void* const* k_pools, void* const* v_pools, int32_t num_layers,
+                          int64_t pool_num_blocks, int64_t block_bytes, const int32_t* ids, int32_t n,
+                          const void* staging, int32_t* error_word, void* stream_ptr, const char* what) {
+  using namespace pa;
+  if (num_layers < 0 || n < 0 || pool_num_blocks <= 0 || block_bytes <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%s: bad sizes (layers %d, count %d, pool %lld blocks of %lld bytes)", what,
+                num_layers, n, (long long)pool_num_blocks, (long long)block_bytes);
+  if (block_bytes % 16 != 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%s: block_bytes %lld is not a multiple of 16", what, (long long)block_bytes);
+  if (n == 0 || num_layers == 0) return PA_OK;
+  if (!k_pools || !v_pools || !ids || !error_word || (mode != kBlockCopy && !staging))
+    return fail(PA_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  if (reinterpret_cast<uintptr_t>(staging) % 16 != 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%s: staging buffer is not 16-byte aligned", what);
+  BlockCopyParams p{};
+  p.mode = mode;
+  p.n = n;
+  p.block_bytes = block_bytes;
+  p.pool_blocks = pool_num_blocks;
+  p.ids = ids;
+  p.staging = static_cast<uint8_t*>(const_cast<void*>(staging));
+  p.err = error_word;
+  for (int32_t l0 = 0; l0 < num_layers; l0 += kCopyLayers) {
+    p.layer0 = l0;
+    p.num_layers = std::min<int32_t>(kCopyLayers, num_layers - l0);
+    for (int32_t l = 0; l < p.num_layers; ++l) {
+      p.k[l] = static_cast<uint8_t*>(k_pools[l0 + l]);
+      p.v[l] = static_cast<uint8_t*>(v_pools[l0 + l]);
+      if (!p.k[l] || !p.v[l] || reinterpret_cast<uintptr_t>(p.k[l]) % 16 || reinterpret_cast<uintptr_t>(p.v[l]) % 16)
+        return fail(PA_ERR_INVALID_ARGUMENT, "%s: layer %d pool pointer is NULL or not 16-byte aligned", what, l0 + l);
+    }
+    cudaError_t e = launch_block_copy(p, static_cast<cudaStream_t>(stream_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, what);
+  }
+  return PA_OK;
+}
+
+int32_t pa_copy_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                       int64_t block_bytes, const int32_t* pairs, int32_t num_pairs, int32_t* error_word,
+                       void* stream) {
+  return block_move(pa::kBlockCopy, k_pools, v_pools, num_layers, pool_num_blocks, block_bytes, pairs, num_pairs,
+                    nullptr, error_word, stream, "copy_blocks");
+}
+
+int32_t pa_gather_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                         int64_t block_bytes, const int32_t* blocks, int32_t num_blocks, void* staging,
+                         int32_t* error_word, void* stream) {
+  return block_move(pa::kBlockGather, k_pools, v_pools, num_layers, pool_num_blocks, block_bytes, blocks, num_blocks,
+                    staging, error_word, stream, "gather_blocks");
+}
+
+int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t num_layers, int64_t pool_num_blocks,
+                          int64_t block_bytes, const int32_t* blocks, int32_t num_blocks, const void* staging,
+                          int32_t* error_word, void* stream) {
+  return block_move(pa::kBlockScatter, k_pools, v_pools, num_layers, pool_num_blocks, block_bytes, blocks,
+                    num_blocks, staging, error_word, stream, "scatter_blocks");
 }
 
 int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream_ptr) {

@@ -95,6 +95,23 @@ struct AppendParams {
   const int32_t* slots;
 };
 
+// Whole-block moves over every layer's K and V pools (copy-on-write, swap gather/scatter).
+constexpr int kCopyLayers = 128;  // layers per launch (pool pointers travel in the parameters)
+enum BlockMoveMode : int32_t { kBlockCopy = 0, kBlockGather = 1, kBlockScatter = 2 };
+struct BlockCopyParams {
+  uint8_t* k[kCopyLayers];
+  uint8_t* v[kCopyLayers];
+  int32_t num_layers;         // layers in this launch
+  int32_t layer0;             // index of k[0] among all layers (staging offset)
+  int32_t mode;               // BlockMoveMode
+  int32_t n;                  // pairs (copy) or blocks (gather / scatter)
+  int64_t block_bytes;        // block_size * Hkv * D * element size, a multiple of 16
+  int64_t pool_blocks;
+  const int32_t* ids;         // copy: [n][2] (src, dst); gather / scatter: [n]
+  uint8_t* staging;           // [all layers][K, V][n][block_bytes]
+  int* err;
+};
+
 // Returns true when the fast decode kernel has an instantiation for this shape.
 bool decode_supported(int dtype, int head_dim, int group, int block_size);
 // Dynamic shared memory bytes of the decode kernel.
@@ -113,5 +130,6 @@ int prefill_tile_rows();
 cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
                               const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
+cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 
 }  // namespace pa

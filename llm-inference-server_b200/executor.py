@@ -33,7 +33,7 @@ import torch
 from transformers import AttentionInterface, Cache
 
 from .attention import paged_attention_cuda
-from .kv_cache import reshape_and_cache
+from .kv_cache import copy_blocks, reshape_and_cache
 from .metadata import StepMetadata, attach, prefill_tile_tokens
 
 #: Name under which the CUDA attention is registered with transformers while a paged
@@ -166,11 +166,8 @@ class CudaPagedExecutor:
 
     def _copy_block(self, src: int, dst: int) -> None:
         """Move one block's K/V, every layer, for ``BlockTable.ensure_private``
-        (paged_executor.py:265-270)."""
-        for layer in self.pool.k:
-            layer[dst].copy_(layer[src])
-        for layer in self.pool.v:
-            layer[dst].copy_(layer[src])
+        (paged_executor.py:265-270): one block-copy launch for all layers."""
+        copy_blocks(self.pool.k, self.pool.v, [(src, dst)])
 
     # ------------------------------------------------------------------ forward
     def _forward(self, input_ids, position_ids, ctx: StepContext):

@@ -18,6 +18,9 @@ integer arithmetic around it.  Every function cites the reference file:line it f
   slots                  inference_server/core/block_table.py:143-159 (BlockTable.slots)
   pack_step              inference_server/core/paged_executor.py:211-263 (_pack)
   kv_append              inference_server/core/paged_executor.py:116-125 (_PagedCache.update)
+  swap_out               inference_server/core/kv_pool.py:142-166 (PagedKVPool.swap_out)
+  swap_in                inference_server/core/kv_pool.py:168-182 (PagedKVPool.swap_in)
+  copy_block             inference_server/core/paged_executor.py:265-270 (_copy_block)
 
 Parity is pinned: ``tests/golden/make_golden.py`` runs the reference itself (imported
 from its source tree in the development container) on seeded inputs and commits its
@@ -248,3 +251,36 @@ def kv_append(pool: np.ndarray, write_slots, new: np.ndarray) -> np.ndarray:
     flat = out.reshape(-1, *out.shape[2:])
     flat[np.asarray(write_slots, dtype=np.int64)] = new
     return out
+
+
+def swap_out(k_layers: np.ndarray, v_layers: np.ndarray, blocks) -> tuple[np.ndarray, np.ndarray]:
+    """Per-layer ``index_select(0, blocks)`` of K and V (kv_pool.py:142-166).
+
+    k_layers / v_layers [L, NB, BS, Hkv, D] (any dtype, bitwise); returns the host copies
+    [L, n, BS, Hkv, D] for K and V.
+    """
+    idx = np.asarray(blocks, dtype=np.int64)
+    return np.array(k_layers[:, idx], copy=True), np.array(v_layers[:, idx], copy=True)
+
+
+def swap_in(k_layers: np.ndarray, v_layers: np.ndarray, host_k: np.ndarray, host_v: np.ndarray,
+            blocks) -> tuple[np.ndarray, np.ndarray]:
+    """Per-layer ``index_copy_(0, blocks, host)`` (kv_pool.py:168-182), with its length
+    check; returns the updated pools (copies)."""
+    if len(blocks) != host_k.shape[1]:
+        raise ValueError(f"swap_in: {host_k.shape[1]} host blocks into {len(blocks)} device blocks")
+    k, v = np.array(k_layers, copy=True), np.array(v_layers, copy=True)
+    idx = np.asarray(blocks, dtype=np.int64)
+    k[:, idx] = host_k
+    v[:, idx] = host_v
+    return k, v
+
+
+def copy_block(k_layers: np.ndarray, v_layers: np.ndarray, pairs) -> tuple[np.ndarray, np.ndarray]:
+    """``layer[dst].copy_(layer[src])`` for every layer, K then V, pair by pair in order
+    (paged_executor.py:265-270); returns the updated pools (copies)."""
+    k, v = np.array(k_layers, copy=True), np.array(v_layers, copy=True)
+    for src, dst in pairs:
+        k[:, dst] = k[:, src]
+        v[:, dst] = v[:, src]
+    return k, v

@@ -18,6 +18,9 @@ What it records, all from the reference's own code on CPU:
   tables, context/query lengths, position ids.
 * ``kv_append_<dtype>.npz``: pool contents after ``_PagedCache.update``
   (paged_executor.py:116-125).
+* ``blocks_<dtype>.npz``: block moves of a 3-layer pool: ``PagedKVPool.swap_out`` /
+  ``swap_in`` (kv_pool.py:142-182) and ``PagedExecutor._copy_block``
+  (paged_executor.py:265-270).
 * ``gpt2_greedy_cpu.npz``: greedy tokens of the reference's own ``PagedExecutor`` with
   the gather path (paged_executor.py:162-295) on CPU, driving a random-init GPT-2 124M
   (``GPT2LMHeadModel(GPT2Config())`` after ``torch.manual_seed(0)``, fp32) over three
@@ -114,9 +117,9 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the llm-inference-server checkout")
     ap.add_argument("--only", nargs="*", default=None,
-                    help="regenerate only these outputs: attn token_map pack kv_append gpt2_greedy")
+                    help="regenerate only these outputs: attn token_map pack kv_append blocks gpt2_greedy")
     args = ap.parse_args()
-    want = set(args.only) if args.only else {"attn", "token_map", "pack", "kv_append", "gpt2_greedy"}
+    want = set(args.only) if args.only else {"attn", "token_map", "pack", "kv_append", "blocks", "gpt2_greedy"}
     os.environ.setdefault("DEVICE", "cpu")
     sys.path.insert(0, str(Path(args.reference).resolve()))
 
@@ -142,6 +145,8 @@ def main() -> None:
 
     if "gpt2_greedy" in want:
         _gpt2_greedy(PagedExecutor, PagedKVPool, ModelDims, BlockAllocator, BlockTable, Sequence)
+    if "blocks" in want:
+        _blocks(PagedExecutor, PagedKVPool, ModelDims)
     if not want & {"token_map", "pack", "kv_append"}:
         return
 
@@ -211,6 +216,36 @@ def main() -> None:
             k_after=_store(pool.k[1], dt), v_after=_store(pool.v[1], dt), dtype=np.bytes_(dt),
         )
     print(f"wrote {len(CASES)} attention cases + token_map, pack, kv_append to {HERE}")
+
+
+def _blocks(PagedExecutor, PagedKVPool, ModelDims) -> None:
+    """Swap-out, swap-in and copy-on-write moves of the reference pool (CPU)."""
+    for dt in ("f32", "bf16"):
+        td = TORCH_DTYPE[dt]
+        g = torch.Generator().manual_seed(23)
+        pool = PagedKVPool(ModelDims(3, 2, 8, td), num_blocks=16, block_size=4, device="cpu")
+        for layer in range(3):
+            pool.k[layer].copy_(torch.randn(pool.k[layer].shape, generator=g).to(td))
+            pool.v[layer].copy_(torch.randn(pool.v[layer].shape, generator=g).to(td))
+        k0 = torch.stack(pool.k).clone()
+        v0 = torch.stack(pool.v).clone()
+        out_blocks, in_blocks = [5, 2, 11, 7], [0, 9, 3, 14]
+        host = pool.swap_out(out_blocks)
+        pool.swap_in(host, in_blocks)
+        k1, v1 = torch.stack(pool.k).clone(), torch.stack(pool.v).clone()
+        ex = PagedExecutor(model=None, tokenizer=None, pool=pool)
+        pairs = [(4, 12), (1, 6), (9, 15)]
+        for src, dst in pairs:
+            ex._copy_block(src, dst)
+        np.savez_compressed(
+            HERE / f"blocks_{dt}.npz",
+            k_before=_store(k0, dt), v_before=_store(v0, dt),
+            swap_out_blocks=np.array(out_blocks), host_k=_store(torch.stack(host.k), dt),
+            host_v=_store(torch.stack(host.v), dt), swap_in_blocks=np.array(in_blocks),
+            k_after_swap_in=_store(k1, dt), v_after_swap_in=_store(v1, dt),
+            copy_pairs=np.array(pairs), k_after_copy=_store(torch.stack(pool.k), dt),
+            v_after_copy=_store(torch.stack(pool.v), dt), dtype=np.bytes_(dt),
+        )
 
 
 def _gpt2_greedy(PagedExecutor, PagedKVPool, ModelDims, BlockAllocator, BlockTable, Sequence) -> None:

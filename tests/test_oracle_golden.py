@@ -73,6 +73,24 @@ def test_kv_append_matches_reference(dt, oracle):
     np.testing.assert_array_equal(oracle.kv_append(z["v_before"], z["write_slots"], val), z["v_after"])
 
 
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_block_moves_match_reference(dt, oracle):
+    """swap_out / swap_in (kv_pool.py:142-182) and _copy_block (paged_executor.py:265-270)
+    of the reference pool, bit for bit (half dtypes compared as raw patterns)."""
+    z = load(f"blocks_{dt}")
+    hk, hv = oracle.swap_out(z["k_before"], z["v_before"], z["swap_out_blocks"])
+    np.testing.assert_array_equal(hk, z["host_k"])
+    np.testing.assert_array_equal(hv, z["host_v"])
+    k1, v1 = oracle.swap_in(z["k_before"], z["v_before"], hk, hv, z["swap_in_blocks"])
+    np.testing.assert_array_equal(k1, z["k_after_swap_in"])
+    np.testing.assert_array_equal(v1, z["v_after_swap_in"])
+    k2, v2 = oracle.copy_block(k1, v1, z["copy_pairs"].tolist())
+    np.testing.assert_array_equal(k2, z["k_after_copy"])
+    np.testing.assert_array_equal(v2, z["v_after_copy"])
+    with pytest.raises(ValueError, match="host blocks into"):
+        oracle.swap_in(z["k_before"], z["v_before"], hk, hv, z["swap_in_blocks"][:-1])
+
+
 def test_slots_raise_past_capacity(oracle):
     with pytest.raises(IndexError):
         oracle.slots([3, 1], 16, 33)
