@@ -302,7 +302,300 @@ WORKLOADS = {
                         lo=16, hi=8192, layers=1, churn=0.0),
     "config2-bf16": dict(heads=12, kv_heads=12, head_dim=64, dtype="bf16", mean_ctx=0.0, median_ctx=1024.0,
                          lo=16, hi=8192, layers=1, churn=0.0),
+    # Llama-3-70B-shape decode with KV heads sharded over the GPUs
+    # (--gpus N = tensor-parallel size), o_proj row-split, one all-reduce per layer.
+    "config5": dict(heads=64, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=8192.0, median_ctx=None,
+                    lo=128, hi=32768, layers=80, churn=0.0, batch=512, d_model=8192),
+    # Whole-block moves on the config-3 pool shape: copy-on-write and swap-out / swap-in.
+    "blocks": dict(heads=32, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=0.0, median_ctx=None,
+                   lo=0, hi=0, layers=32, churn=0.0),
 }
+
+def run_tp(args, rank: int, world: int, local_rank: int) -> None:
+    """``--workload config5``: BASELINE config 5 decode (Llama-3-70B attention shape: 64 q
+    / 8 kv heads, head_dim 128, bf16, 80 layers, d_model 8192, batch 512, contexts
+    lognormal mean 8192 clipped 128..32768) with the KV heads sharded over the
+    ``--gpus N`` ranks (tensor_parallel.KVHeadParallelAttention: fused append, paged
+    attention over the rank's heads, the rank's row slice of o_proj, one NCCL all-reduce
+    of [batch, d_model] per layer).  Every rank serves the same batch, so the total work
+    is fixed (``scaling: strong``).  The 80 layer calls cycle over as many physical
+    per-layer pools as fit in 55 % of HBM (layer l uses pool l mod P); each call still
+    streams its whole KV (GBs, far above L2) and appends its own new tokens."""
+    import importlib
+
+    from __graft_entry__ import import_package
+
+    pkg = import_package()
+    tpm = importlib.import_module(f"{pkg.__name__}.tensor_parallel")
+    w = WORKLOADS["config5"]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if w["kv_heads"] % world:
+        raise SystemExit(f"config5 shards {w['kv_heads']} KV heads; {world} ranks do not divide them")
+    L, B, D, DM = args.layers, args.batch, w["head_dim"], w["d_model"]
+    steps_total = args.warmup + args.steps
+    wl = Workload(batch=B, layers=L, heads=w["heads"], kv_heads=w["kv_heads"], head_dim=D, block_size=16,
+                  mean_ctx=w["mean_ctx"], lo=w["lo"], hi=w["hi"], sigma=0.9, seed=args.seed, max_steps=steps_total + 1,
+                  churn=0.0)
+    qs, ks = tpm.kv_head_shard(w["heads"], w["kv_heads"], rank, world)
+    Hq, Hkv = qs.stop - qs.start, ks.stop - ks.start
+    per_layer = wl.num_blocks * 16 * Hkv * D * 2 * 2
+    P = max(1, min(L, int(0.55 * torch.cuda.get_device_properties(dev).total_memory // per_layer)))
+    g = torch.Generator(device=dev).manual_seed(args.seed + 100 * rank)
+    shape = (wl.num_blocks, 16, Hkv, D)
+    k_pools = [torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=g) for _ in range(P)]
+    v_pools = [torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=g) for _ in range(P)]
+    q = [torch.randn(B, Hq, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(L)]
+    kn = [torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(L)]
+    vn = [torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(L)]
+    w_o = [(torch.randn(Hq * D, DM, generator=g, device=dev) / (w["heads"] * D) ** 0.5).to(torch.bfloat16)
+           for _ in range(L)]
+    bt = torch.from_numpy(wl.tables).to(dev)
+    sm = pkg.metadata.sm_count(dev)
+    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
+    dummy = torch.zeros(1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def plan(s):
+        return pkg.StepMetadata.plan_host(wl.context_lens(s), wl.query_lens, wl.tables, num_tokens=B,
+                                          pool_num_blocks=wl.num_blocks, block_size=16, num_kv_heads=Hkv, sm=sm,
+                                          prefill_tile_tokens=tile, pinned=True)
+
+    metas = [plan(s).upload(dev) for s in range(steps_total)]
+    layers = [tpm.KVHeadParallelAttention(w_o=w_o[l]) for l in range(L)]
+
+    def step(meta, marks=None, host=None):
+        slots = meta.slot_mapping()
+        bta = pkg.attach(bt, meta)
+        out = None
+        for l in range(L):
+            if host is not None:   # e2e: this layer's q / new K / new V come from pinned host memory
+                q[0].copy_(host[0], non_blocking=True)
+                kn[0].copy_(host[1], non_blocking=True)
+                vn[0].copy_(host[2], non_blocking=True)
+                ql, kl, vl = q[0], kn[0], vn[0]
+            else:
+                ql, kl, vl = q[l], kn[l], vn[l]
+            kp, vp = k_pools[l % P], v_pools[l % P]
+            if marks is not None:
+                marks[l][0].record(stream)
+            pkg.reshape_and_cache(kl, vl, kp, vp, slots)
+            attn = pkg.paged_attention_cuda(ql, kp, vp, bta, dummy, dummy, D ** -0.5)
+            if marks is not None:
+                marks[l][1].record(stream)
+            partial = attn.reshape(B, -1) @ layers[l].w_o
+            if marks is not None:
+                marks[l][2].record(stream)
+            if world > 1:
+                torch.distributed.all_reduce(partial)
+            if marks is not None:
+                marks[l][3].record(stream)
+            out = partial
+        return out
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    clocks = ClockSampler(dev.index)
+    with clocks:
+        for s in range(args.warmup):
+            step(metas[s])
+        barrier()
+        torch.cuda.synchronize(dev)
+        marks = [[[ev() for _ in range(4)] for _ in range(L)] for _ in range(args.steps)]
+        t0, t1 = ev(), ev()
+        t0.record(stream)
+        for k in range(args.steps):
+            step(metas[args.warmup + k], marks[k])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        elapsed = t0.elapsed_time(t1)
+        attn_kernels = pkg._lib.last_launches()      # this library's kernels per attention call
+        attn_ms = float(np.mean([m[0].elapsed_time(m[1]) for mk in marks for m in mk]))
+        gemm_ms = float(np.mean([m[1].elapsed_time(m[2]) for mk in marks for m in mk]))
+        ar_ms = float(np.mean([m[2].elapsed_time(m[3]) for mk in marks for m in mk]))
+
+        # e2e: metadata planned and uploaded every step, each layer's inputs from pinned
+        # host memory, the step's output (last layer, [batch, d_model]) read back.
+        host = [q[0].cpu().pin_memory(), kn[0].cpu().pin_memory(), vn[0].cpu().pin_memory()]
+        out_host = torch.empty(B, DM, dtype=torch.bfloat16).pin_memory()
+        for s in range(args.warmup):
+            out_host.copy_(step(plan(s).upload(dev), host=host), non_blocking=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        words = 0
+        for k in range(args.steps):
+            m = plan(args.warmup + k)
+            words += int(m.plan.words)
+            out_host.copy_(step(m.upload(dev), host=host), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+    assert pkg.read_device_error(dev) == 0, "a kernel set the device error word"
+    times = torch.tensor([elapsed, e2e_ms, attn_ms, gemm_ms, ar_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    elapsed, e2e_ms, attn_ms, gemm_ms, ar_ms = times.tolist()
+    if rank != 0:
+        return
+    timed = [args.warmup + k for k in range(args.steps)]
+    ctx_sum = float(np.mean([wl.context_lens(s).sum() for s in timed]))
+    attn_bytes = (ctx_sum * Hkv * D * 2 * 2 + 2 * B * Hq * D * 2 + ctx_sum / 16 * 4 + 2 * B * Hkv * D * 2 * 2)
+    hbm_peak, bf16_peak, peak_kind = _measured_peaks()
+    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    ar_bytes = B * DM * 2
+    line = {
+        "metric": METRIC, "value": B * args.steps / (elapsed / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 5: Llama-3-70B-shape GQA decode (64 q / 8 kv heads, head_dim 128, "
+                               f"bf16, {L} layers, d_model {DM}), batch {B}, contexts lognormal mean 8192 clipped "
+                               f"128..32768, KV heads sharded over {world} GPU(s) with a row-split o_proj and one "
+                               "all-reduce per layer",
+                   "model": "llama3-70b-shape attention + o_proj (random-init)", "global_batch": B, "layers": L,
+                   "kv_heads_per_gpu": Hkv, "q_heads_per_gpu": Hq, "sum_context_step0": int(wl.ctx0.sum()),
+                   "seq_len": "ragged (mean 8192)", "physical_layer_pools": P,
+                   "l2": f"each layer call streams {per_layer / 1e9:.2f} GB of KV (>> 126 MB L2); {L} layer calls "
+                         f"cycle over {P} physical pools",
+                   "parallelism": f"tp{world} (KV-head sharding; NCCL all-reduce after o_proj)" if world > 1 else "tp1"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy", "traffic": None,
+                     "kernel": "per-rank KV append + decode paged attention per layer (tensor-pipe MMA + combine)",
+                     "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
+        "o_proj": {"avg_ms": gemm_ms, "tflops": 2 * B * Hq * D * DM / (gemm_ms / 1e3) / 1e12,
+                   "peak_tflops": bf16_peak, "kernel": "torch bf16 matmul (cuBLAS)"},
+        "all_reduce": None if world == 1 else {
+            "avg_ms": ar_ms, "bytes": ar_bytes, "bus_gbs": 2 * (world - 1) / world * ar_bytes / (ar_ms / 1e3) / 1e9,
+            "backend": "NCCL"},
+        "cpu_baseline": None,
+        "e2e": {"value": B * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": words * 4 // args.steps + L * B * (Hq + 2 * Hkv) * D * 2,
+                "d2h_bytes_per_step": B * DM * 2, "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": args.steps * L * (1 + len(attn_kernels)),
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+BLOCK_POOL_BLOCKS = 16384   # per layer: 16384 x [16, 8, 128] bf16 = 512 MB for K and V
+BLOCK_COW_PAIRS = 256       # copy-on-write pairs per step
+BLOCK_SWAP = 64             # blocks swapped out and back in per step (a 1,024-token sequence)
+
+
+def _blocks_cpu_sample(args) -> dict:
+    """The oracle's copy_block (the reference's per-layer block copies, in numpy) on a
+    host-sized sample of the blocks workload: GB/s read + written."""
+    from oracle import paged_attention_oracle as oracle
+
+    block_bytes = 16 * WORKLOADS["blocks"]["kv_heads"] * WORKLOADS["blocks"]["head_dim"] * 2
+    ks = np.zeros((4, 2048, block_bytes // 2), dtype=np.uint16)
+    vs = np.zeros_like(ks)
+    pairs = list(zip(range(0, 128), range(1024, 1152)))
+    reps, t_end = [], time.perf_counter() + min(args.cpu_budget_s, 5.0)
+    while len(reps) < 3 or time.perf_counter() < t_end:
+        a = time.perf_counter()
+        oracle.copy_block(ks, vs, pairs)
+        reps.append(time.perf_counter() - a)
+    moved = 2 * len(pairs) * 4 * 2 * block_bytes
+    return {"value": moved / float(np.median(reps)) / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"oracle copy_block: {len(pairs)} pairs x 4 layers x K,V of {block_bytes} B blocks (the "
+                      f"reference's per-layer copies, numpy), {len(reps)} repetitions; includes the oracle's "
+                      "copy of the input pools"}
+
+
+def run_blocks(args, rank: int, world: int, local_rank: int) -> None:
+    """``--workload blocks``: one step = copy-on-write of BLOCK_COW_PAIRS blocks in every
+    layer (one launch), then swap-out of BLOCK_SWAP blocks to pinned host memory and
+    swap-in into other blocks (kv_pool.py:142-182's operations, one gather / scatter
+    launch and one PCIe copy each).  ``value`` = copy-on-write GB/s (bytes read + written
+    by the device-resident copy kernel); ``e2e`` = swap round-trip GB/s over PCIe."""
+    from __graft_entry__ import import_package
+
+    pkg = import_package()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = WORKLOADS["blocks"]
+    L, NB, P, S = args.layers, BLOCK_POOL_BLOCKS, BLOCK_COW_PAIRS, BLOCK_SWAP
+    pool = pkg.KVPool(L, NB, 16, w["kv_heads"], w["head_dim"], torch.bfloat16, dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    for t in pool.k + pool.v:
+        t.normal_(generator=g)
+    block_bytes = 16 * w["kv_heads"] * w["head_dim"] * 2
+    rng = np.random.default_rng(args.seed + rank)
+    plans = []
+    for _ in range(args.warmup + args.steps):
+        perm = rng.permutation(NB).tolist()
+        plans.append((list(zip(perm[:P], perm[P:2 * P])), perm[2 * P:2 * P + S], perm[2 * P + S:2 * P + 2 * S]))
+    copy_bytes = 2 * P * L * 2 * block_bytes      # read + write
+    swap_bytes = S * L * 2 * block_bytes          # each direction
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def step(s, marks=None):
+        pairs, out_b, in_b = plans[s]
+        if marks:
+            marks[0].record(stream)
+        pool.copy_blocks(pairs)
+        if marks:
+            marks[1].record(stream)
+        host = pool.swap_out(out_b)
+        if marks:
+            marks[2].record(stream)
+        pool.swap_in(host, in_b)
+        if marks:
+            marks[3].record(stream)
+
+    clocks = ClockSampler(dev.index)
+    with clocks:
+        for s in range(args.warmup):
+            step(s)
+        torch.cuda.synchronize(dev)
+        marks = [[ev() for _ in range(4)] for _ in range(args.steps)]
+        t0, t1 = ev(), ev()
+        t0.record(stream)
+        for k in range(args.steps):
+            step(args.warmup + k, marks[k])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    assert pool.read_error() == 0
+    total_ms = t0.elapsed_time(t1)
+    cow_ms = float(np.mean([m[0].elapsed_time(m[1]) for m in marks]))
+    out_ms = float(np.mean([m[1].elapsed_time(m[2]) for m in marks]))
+    in_ms = float(np.mean([m[2].elapsed_time(m[3]) for m in marks]))
+    if rank != 0:
+        return
+    hbm_peak, _, peak_kind = _measured_peaks()
+    achieved = copy_bytes / (cow_ms / 1e3) / 1e9
+
+    cpu = _blocks_cpu_sample(args) if world == 1 and not args.no_cpu_baseline else None
+    line = {
+        "metric": "KV block moves: copy-on-write GB/s (device) and swap round trip GB/s (PCIe)",
+        "value": achieved, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"block moves on the Llama-3-8B pool shape: {L} layers x {NB} blocks of "
+                               f"[16, 8, 128] bf16; per step {P} copy-on-write pairs, {S} blocks swapped out "
+                               "and back into other blocks", "layers": L, "pool_blocks": NB,
+                   "cow_pairs": P, "swap_blocks": S, "l2": "each step moves >= 0.5 GB, far above the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy", "traffic": None,
+                     "kernel": "block_copy_kernel (copy-on-write, all layers in one launch)",
+                     "algorithmic_bytes_per_launch": copy_bytes, "avg_launch_ms": cow_ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": 2 * swap_bytes / ((out_ms + in_ms) / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": swap_bytes, "d2h_bytes_per_step": swap_bytes,
+                "swap_out_ms": out_ms, "swap_in_ms": in_ms,
+                "swap_out_gbs": swap_bytes / (out_ms / 1e3) / 1e9, "swap_in_gbs": swap_bytes / (in_ms / 1e3) / 1e9},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
 
 
 def _make_workload(args, rank: int, max_steps: int) -> Workload:
@@ -577,19 +870,23 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=None, help="default: the workload's (256; 512 for config5)")
     ap.add_argument("--layers", type=int, default=None, help="default: the workload's (32 for config3)")
     ap.add_argument("--churn", type=float, default=None,
                     help="fraction of the batch re-admitted per step (default: the workload's, 0.05 for config3)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
-                    help="config3 (default headline) or BASELINE config 2's isolated decode microbenchmark")
+                    help="config3 (default headline), BASELINE config 2's isolated decode microbenchmark, "
+                         "config5 (70B shape, KV heads sharded over --gpus), or blocks (copy-on-write and swap "
+                         "moves)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.layers is None:
         args.layers = WORKLOADS[args.workload]["layers"]
+    if args.batch is None:
+        args.batch = WORKLOADS[args.workload].get("batch", 256)
     if args.churn is None:
         args.churn = WORKLOADS[args.workload]["churn"]
     if args.warmup < 3:
@@ -610,7 +907,20 @@ def main() -> None:
             torch.distributed.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     try:
         if args.impl == "reference":
-            run_reference(args, rank, world)
+            if args.workload == "blocks":
+                if rank == 0:
+                    cpu = _blocks_cpu_sample(args)
+                    print(json.dumps({"impl": "reference", "metric": "KV block moves: copy-on-write GB/s (device) "
+                                      "and swap round trip GB/s (PCIe)", "value": cpu["value"], "unit": "GB/s",
+                                      "n_gpus": world, "higher_is_better": True, "cpu_baseline": cpu,
+                                      "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                              "d2h_bytes_per_step": 0}}), flush=True)
+            else:
+                run_reference(args, rank, world)
+        elif args.workload == "blocks":
+            run_blocks(args, rank, world, local_rank)
+        elif args.workload == "config5":
+            run_tp(args, rank, world, local_rank)
         else:
             run_cuda(args, rank, world, local_rank)
     finally:

@@ -50,8 +50,19 @@ __global__ void __launch_bounds__(256) block_copy_kernel(const BlockCopyParams p
     src = reinterpret_cast<const uint4*>(p.mode == kBlockGather ? blk : stage);
     dst = reinterpret_cast<uint4*>(p.mode == kBlockGather ? stage : blk);
   }
+  // Eight 16-byte loads in flight per thread before their stores (a 32 KB block is
+  // exactly one such round at 256 threads).
   const int64_t chunks = p.block_bytes / 16;
-  for (int64_t c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = src[c];
+  const int64_t step = blockDim.x;
+  int64_t c = threadIdx.x;
+  for (; c + 7 * step < chunks; c += 8 * step) {
+    uint4 r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) r[u] = src[c + u * step];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) dst[c + u * step] = r[u];
+  }
+  for (; c < chunks; c += step) dst[c] = src[c];
 }
 
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream) {
