@@ -364,6 +364,8 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
 
     metas = [plan(s).upload(dev) for s in range(steps_total)]
     layers = [tpm.KVHeadParallelAttention(w_o=w_o[l]) for l in range(L)]
+    reducer = (tpm.PeerAllReduce(B * DM, torch.bfloat16, device=dev, timeout_s=10.0)
+               if world > 1 and args.allreduce == "peer" else None)
 
     def step(meta, marks=None, host=None):
         slots = meta.slot_mapping()
@@ -384,10 +386,16 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
             attn = pkg.paged_attention_cuda(ql, kp, vp, bta, dummy, dummy, D ** -0.5)
             if marks is not None:
                 marks[l][1].record(stream)
-            partial = attn.reshape(B, -1) @ layers[l].w_o
+            a2 = attn.reshape(B, -1)
+            if reducer is not None:   # the GEMM writes into the peer-mapped slot
+                partial = torch.matmul(a2, layers[l].w_o, out=reducer.slot((B, DM)))
+            else:
+                partial = a2 @ layers[l].w_o
             if marks is not None:
                 marks[l][2].record(stream)
-            if world > 1:
+            if reducer is not None:
+                reducer.all_reduce_(partial)
+            elif world > 1:
                 torch.distributed.all_reduce(partial)
             if marks is not None:
                 marks[l][3].record(stream)
@@ -438,6 +446,10 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
         barrier()
         e2e_ms = e0.elapsed_time(e1)
     assert pkg.read_device_error(dev) == 0, "a kernel set the device error word"
+    if reducer is not None:
+        reducer.check()
+        reducer.close()
+        barrier()
     times = torch.tensor([elapsed, e2e_ms, attn_ms, gemm_ms, ar_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
@@ -463,7 +475,8 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
                    "seq_len": "ragged (mean 8192)", "physical_layer_pools": P,
                    "l2": f"each layer call streams {per_layer / 1e9:.2f} GB of KV (>> 126 MB L2); {L} layer calls "
                          f"cycle over {P} physical pools",
-                   "parallelism": f"tp{world} (KV-head sharding; NCCL all-reduce after o_proj)" if world > 1 else "tp1"},
+                   "parallelism": (f"tp{world} (KV-head sharding; {'peer-memory' if reducer is not None else 'NCCL'} "
+                                   "all-reduce after o_proj)") if world > 1 else "tp1"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy", "traffic": None,
                      "kernel": "per-rank KV append + decode paged attention per layer (tensor-pipe MMA + combine)",
@@ -472,12 +485,13 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
                    "peak_tflops": bf16_peak, "kernel": "torch bf16 matmul (cuBLAS)"},
         "all_reduce": None if world == 1 else {
             "avg_ms": ar_ms, "bytes": ar_bytes, "bus_gbs": 2 * (world - 1) / world * ar_bytes / (ar_ms / 1e3) / 1e9,
-            "backend": "NCCL"},
+            "backend": "NCCL" if reducer is None else "peer memory (pa_peer_allreduce: two-shot over NVLink, "
+                                                        "GEMM output written into the peer-mapped slot)"},
         "cpu_baseline": None,
         "e2e": {"value": B * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": words * 4 // args.steps + L * B * (Hq + 2 * Hkv) * D * 2,
                 "d2h_bytes_per_step": B * DM * 2, "ms_per_step": e2e_ms / args.steps},
-        "gpu_launches": args.steps * L * (1 + len(attn_kernels)),
+        "gpu_launches": args.steps * L * (1 + len(attn_kernels) + (1 if reducer is not None else 0)),
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -882,6 +896,8 @@ def main() -> None:
     ap.add_argument("--cpu-sample-seqs", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="config5 at N>1: the o_proj all-reduce over NVLink peer memory (default) or NCCL")
     args = ap.parse_args()
     if args.layers is None:
         args.layers = WORKLOADS[args.workload]["layers"]

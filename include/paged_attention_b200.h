@@ -233,6 +233,44 @@ int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t nu
                           int32_t* error_word, void* stream);
 
 /*
+ * CUDA IPC for the peer all-reduce's buffers (no reference counterpart).
+ * pa_ipc_export: the 64-byte handle of the allocation holding dev_ptr and dev_ptr's byte
+ * offset in it.  pa_ipc_open: map a peer's handle into the calling device's context (peer
+ * access enabled on demand) and return the peer's pointer (allocation base + offset).
+ * pa_ipc_close: unmap a pointer pa_ipc_open returned (same offset).
+ */
+#define PA_IPC_HANDLE_BYTES 64
+int32_t pa_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int32_t pa_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out);
+int32_t pa_ipc_close(void* dev_ptr, int64_t offset);
+
+/*
+ * Sum `count` elements across the `world` ranks of one node (<= 8) in place, over peer
+ * memory.  No counterpart in the reference, which has no multi-GPU path: it replaces the
+ * torch.distributed.all_reduce that follows the row-split o_proj in KV-head tensor
+ * parallelism.
+ *
+ *   bases         HOST array of `world` device pointers: every rank's buffer, mapped into
+ *                 this process (CUDA IPC), all allocated with the same layout
+ *   data_offset   byte offset of this call's data (the caller's partial, overwritten with
+ *                 the sum on every rank); 16-byte aligned, count * element size a multiple
+ *                 of 16
+ *   flags_offset  byte offset of a zero-initialised 128-byte flag area owned by this
+ *                 collective (it also counts the calls, so a captured CUDA graph of the
+ *                 call replays correctly)
+ *   timeout_s     bound on each of the kernel's two barrier waits; on expiry bit 4 of
+ *                 *error_word is set and the collective (and its buffer) must not be
+ *                 used again
+ *
+ * Every rank must make the same sequence of calls with the same arguments except rank and
+ * the mapping of bases;
+ * the kernel returns on each rank once all ranks' sums are in place.  Asynchronous on
+ * `stream`; the caller's partial must be written before it on that stream.
+ */
+int32_t pa_peer_allreduce(void* const* bases, int32_t world, int32_t rank, int64_t data_offset, int64_t flags_offset,
+                          int64_t count, int32_t dtype, double timeout_s, int32_t* error_word, void* stream);
+
+/*
  * Read (and clear, when clear != 0) the device error word a workspace carries.  It is
  * set by kernels that met an out-of-range block id or slot (the host checks make this
  * unreachable for planned steps) or a pipeline wait that ran out of its iteration

@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class StepPlan(ctypes.Structure):
@@ -100,6 +100,11 @@ _SIGNATURES = {
                                    c_int32, c_void_p, c_void_p, c_void_p]),
     "pa_scatter_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p,
                                     c_int32, c_void_p, c_void_p, c_void_p]),
+    "pa_peer_allreduce": (c_int32, [POINTER(c_void_p), c_int32, c_int32, c_int64, c_int64, c_int64, c_int32,
+                                    ctypes.c_double, c_void_p, c_void_p]),
+    "pa_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
+    "pa_ipc_open": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),
+    "pa_ipc_close": (c_int32, [c_void_p, c_int64]),
 }
 
 _lib = None

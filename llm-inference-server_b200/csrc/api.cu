@@ -44,6 +44,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// cuMemGetAddressRange (allocation base of a device pointer) through the same route.
+static PFN_cuMemGetAddressRange_v3020 range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(ptr);
+  });
+  return fn;
+}
+
 struct MapKey {
   uintptr_t base;
   int64_t blocks;
@@ -383,6 +397,83 @@ int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t nu
                           int32_t* error_word, void* stream) {
   return block_move(pa::kBlockScatter, k_pools, v_pools, num_layers, pool_num_blocks, block_bytes, blocks,
                     num_blocks, staging, error_word, stream, "scatter_blocks");
+}
+
+int32_t pa_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
+  using namespace pa;
+  if (!dev_ptr || !handle_out || !offset_out) return fail(PA_ERR_INVALID_ARGUMENT, "ipc_export: NULL pointer");
+  auto fn = range_fn();
+  if (!fn) return fail(PA_ERR_CUDA, "cuMemGetAddressRange is not available from the CUDA driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(PA_ERR_INVALID_ARGUMENT, "ipc_export: %p is not device memory", dev_ptr);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<uintptr_t>(dev_ptr) - uintptr_t(base));
+  return PA_OK;
+}
+
+int32_t pa_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out) {
+  using namespace pa;
+  if (!handle || !dev_ptr_out || offset < 0) return fail(PA_ERR_INVALID_ARGUMENT, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *dev_ptr_out = static_cast<uint8_t*>(base) + offset;
+  return PA_OK;
+}
+
+int32_t pa_ipc_close(void* dev_ptr, int64_t offset) {
+  using namespace pa;
+  if (!dev_ptr || offset < 0) return fail(PA_ERR_INVALID_ARGUMENT, "ipc_close: bad argument");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(dev_ptr) - offset);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return PA_OK;
+}
+
+int32_t pa_peer_allreduce(void* const* bases, int32_t world, int32_t rank, int64_t data_offset, int64_t flags_offset,
+                          int64_t count, int32_t dtype, double timeout_s, int32_t* error_word, void* stream_ptr) {
+  using namespace pa;
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(PA_ERR_INVALID_ARGUMENT, "peer_allreduce: rank %d of %d (at most %d ranks)", rank, world, kPeerMax);
+  if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_UNSUPPORTED, "peer_allreduce: dtype code %d", dtype);
+  const int es = elem_size(dtype);
+  if (count < 0 || (count * es) % 16 != 0)
+    return fail(PA_ERR_UNSUPPORTED, "peer_allreduce: %lld elements is not a whole number of 16-byte vectors",
+                (long long)count);
+  if (!bases || !error_word || data_offset % 16 || flags_offset % 16 || data_offset < 0 || flags_offset < 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "peer_allreduce: NULL pointer or unaligned offset");
+  if (!(timeout_s > 0.0) || timeout_s > 600.0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "peer_allreduce: timeout must be in (0, 600] seconds");
+  PeerReduceParams p{};
+  for (int r = 0; r < world; ++r) {
+    p.base[r] = static_cast<uint8_t*>(bases[r]);
+    if (!p.base[r] || reinterpret_cast<uintptr_t>(p.base[r]) % 16)
+      return fail(PA_ERR_INVALID_ARGUMENT, "peer_allreduce: buffer of rank %d is NULL or not 16-byte aligned", r);
+  }
+  p.data_offset = data_offset;
+  p.flags_offset = flags_offset;
+  p.count = count;
+  p.world = world;
+  p.rank = rank;
+  p.timeout_ns = uint64_t(timeout_s * 1e9);
+  p.err = error_word;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // At most one CTA per SM, so every CTA of the call is resident and the barrier's
+  // signalling CTA always runs.
+  const int64_t vecs = count * es / 16, per = (vecs + world - 1) / world;
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(sms, (per + kPeerThreads - 1) / kPeerThreads)));
+  cudaError_t e = launch_peer_allreduce(dtype, p, grid, static_cast<cudaStream_t>(stream_ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allreduce launch");
+  return PA_OK;
 }
 
 int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream_ptr) {

@@ -112,6 +112,23 @@ struct BlockCopyParams {
   int* err;
 };
 
+// All-reduce over peer memory (tensor-parallel o_proj).  Each rank's mapped buffer holds
+// data slots and, at flags_offset, a uint32 flag area: [kPeerReady + p] and
+// [kPeerDone + p] are written by rank p, [kPeerCounter] counts finished CTAs,
+// [kPeerEpoch] holds the last completed call's epoch.
+constexpr int kPeerMax = 8;
+constexpr int kPeerThreads = 512;
+constexpr int kPeerReady = 0, kPeerDone = 8, kPeerCounter = 16, kPeerEpoch = 17, kPeerFlagWords = 32;
+struct PeerReduceParams {
+  uint8_t* base[kPeerMax];    // every rank's buffer, mapped into this process
+  int64_t data_offset;        // byte offset of this call's data slot (16-byte aligned)
+  int64_t flags_offset;       // byte offset of the flag area
+  int64_t count;              // elements; count * element size is a multiple of 16
+  int32_t world, rank;
+  uint64_t timeout_ns;        // bound on every wait
+  int* err;
+};
+
 // Returns true when the fast decode kernel has an instantiation for this shape.
 bool decode_supported(int dtype, int head_dim, int group, int block_size);
 // Dynamic shared memory bytes of the decode kernel.
@@ -131,5 +148,6 @@ cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensor
                               const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
+cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);
 
 }  // namespace pa

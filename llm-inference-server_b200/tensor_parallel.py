@@ -13,6 +13,7 @@ the arithmetic here is the single-device layer's, split by heads.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -44,6 +45,99 @@ def o_proj_shard(weight: torch.Tensor, num_heads: int, head_dim: int, rank: int,
     return weight[:, cols].t().contiguous()
 
 
+class PeerAllReduce:
+    """In-place sum across the ranks of one node over NVLink peer memory (the C ABI's
+    ``pa_peer_allreduce``): the replacement for NCCL after the row-split o_proj.
+
+    Each rank allocates one buffer with ``SLOTS`` data slots of ``max_count`` elements and
+    a flag area, and maps every peer's buffer through CUDA IPC (plain peer loads and
+    stores; no multicast object is created).  A call works on the next slot in turn:
+    :meth:`slot` hands out that slot as a tensor the o_proj GEMM writes its partial into,
+    :meth:`all_reduce_` sums it across ranks in place.  A result stays valid until
+    ``SLOTS`` more calls have been made.  All ranks must make the same sequence of calls.
+    After a barrier wait runs out (a peer did not join within ``timeout_s``),
+    :meth:`check` raises and the object must be discarded."""
+
+    SLOTS = 2
+    FLAG_BYTES = 128
+
+    def __init__(self, max_count: int, dtype: torch.dtype, group=None, device=None, timeout_s: float = 2.0):
+        from . import _lib
+        from .attention import _DTYPE_CODE
+
+        self._lib = _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError(f"peer all-reduce spans at most 8 ranks of one node, got {self.world}")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dtype, self.code = dtype, _DTYPE_CODE[dtype]
+        self.max_count = int(max_count)
+        es = torch.empty(0, dtype=dtype).element_size()
+        self.slot_bytes = -(-self.max_count * es // 256) * 256
+        self.flags_offset = self.SLOTS * self.slot_bytes
+        self.buf = torch.zeros(self.flags_offset + self.FLAG_BYTES, dtype=torch.uint8, device=self.device)
+        torch.cuda.synchronize(self.device)
+        lib = _lib.lib()
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_int64()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.pa_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(offset)))
+            mine = (handle.raw, offset.value)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, mine, group=group)
+            ptrs, self._opened = [], []
+            for r, (h, off) in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.buf.data_ptr())
+                    continue
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.pa_ipc_open(h, off, ctypes.byref(ptr)))  # mapped on this rank's device
+                ptrs.append(ptr.value)
+                self._opened.append((ptr.value, off))
+        self.bases = (ctypes.c_void_p * self.world)(*ptrs)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.timeout_s = float(timeout_s)
+        self._slot = 0
+        dist.barrier(group=group)
+
+    def slot(self, shape) -> torch.Tensor:
+        """The next data slot as a contiguous ``shape`` tensor of this collective's dtype."""
+        n = 1
+        for d in shape:
+            n *= int(d)
+        if n > self.max_count:
+            raise ValueError(f"{n} elements exceed the collective's {self.max_count}")
+        off = self._slot * self.slot_bytes
+        es = torch.empty(0, dtype=self.dtype).element_size()
+        return self.buf[off:off + n * es].view(self.dtype).view(*shape)
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        """Sum ``t`` (the tensor :meth:`slot` returned for this call) across the ranks in place."""
+        off = t.data_ptr() - self.buf.data_ptr()
+        if t.dtype != self.dtype or not t.is_contiguous() or off != self._slot * self.slot_bytes:
+            raise ValueError("all_reduce_ expects the tensor slot() handed out for this call")
+        self._lib.check(self._lib.lib().pa_peer_allreduce(
+            self.bases, self.world, self.rank, off, self.flags_offset, t.numel(), self.code, self.timeout_s,
+            self.err.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+        self._slot = (self._slot + 1) % self.SLOTS
+        return t
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after the last call has completed on every rank)."""
+        torch.cuda.synchronize(self.device)
+        for ptr, off in getattr(self, "_opened", []):
+            self._lib.check(self._lib.lib().pa_ipc_close(ptr, off))
+        self._opened = []
+
+    def check(self) -> None:
+        """Raise if a barrier wait of any call so far ran out (synchronises the device)."""
+        if int(self.err.item()):
+            raise RuntimeError(f"peer all-reduce: rank {self.rank} gave up waiting for its peers "
+                               f"(timeout {self.timeout_s} s); discard this collective")
+
+
 @dataclass
 class KVHeadParallelAttention:
     """One layer's attention hot path on one tensor-parallel rank.
@@ -57,6 +151,7 @@ class KVHeadParallelAttention:
     group: object = None              # torch.distributed process group (None = default)
     attention: object = None
     append: object = None
+    reducer: object = None            # PeerAllReduce: sum over NVLink peer memory instead of NCCL
 
     def __post_init__(self):
         if self.attention is None:
@@ -74,7 +169,11 @@ class KVHeadParallelAttention:
         ``[T, d_model]`` (identical on every rank)."""
         self.append(k_new, v_new, k_pool, v_pool, slot_mapping)
         attn = self.attention(q, k_pool, v_pool, block_tables, context_lens, query_lens, scale)
-        partial = attn.reshape(attn.shape[0], -1).to(self.w_o.dtype) @ self.w_o
+        a2 = attn.reshape(attn.shape[0], -1).to(self.w_o.dtype)
+        if self.reducer is not None:       # the GEMM writes straight into the peer-mapped slot
+            partial = torch.matmul(a2, self.w_o, out=self.reducer.slot((a2.shape[0], self.w_o.shape[1])))
+            return self.reducer.all_reduce_(partial)
+        partial = a2 @ self.w_o
         if dist.is_available() and dist.is_initialized():
             dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
         return partial

@@ -1,0 +1,146 @@
+"""The NVLink peer-memory all-reduce (tensor_parallel.PeerAllReduce, the C ABI's
+pa_peer_allreduce) on two GPUs: its sums are bitwise the float32 rank-order sum rounded
+once, identical on every rank, across repeated calls (epochs and slot reuse); the KV-head
+tensor-parallel layer gives the same result through it as through NCCL; and a peer that
+never joins ends the call with a timeout error instead of a hang.  Skipped with fewer than
+two GPUs.  NVLS is off (NCCL_NVLS_ENABLE=0) and the collective maps peers with plain CUDA
+IPC, so no rank's memory is bound to a multicast object."""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+needs_two = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "tests"))
+    import importlib
+
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    result = {}
+    try:
+        from __graft_entry__ import import_package
+
+        import_package()
+        tp = importlib.import_module("llm_inference_server_b200.tensor_parallel")
+        if mode == "sum":
+            for dtype in (torch.bfloat16, torch.float32):
+                red = tp.PeerAllReduce(512 * 1024, dtype, timeout_s=5.0)
+                for it in range(6):
+                    rows = 512 if it % 2 == 0 else 200       # a partial slot: the sum covers 200 x 1024 only
+                    parts = [torch.randn(rows, 1024, generator=torch.Generator().manual_seed(100 * it + r)).to(dtype)
+                             for r in range(world)]
+                    t = red.slot((rows, 1024))
+                    t.copy_(parts[rank].to(dev))
+                    red.all_reduce_(t)
+                    ref = torch.zeros(rows, 1024, dtype=torch.float32)
+                    for p in parts:
+                        ref += p.float()
+                    torch.cuda.synchronize(dev)
+                    got = t.cpu()
+                    key = f"{dtype}-{it}"
+                    result[key] = bool(torch.equal(got, ref.to(dtype)))
+                    np.save(os.path.join(out_dir, f"r{rank}-{key}.npy"), got.float().numpy())
+                red.check()
+                red.close()
+                dist.barrier()
+        elif mode == "layer":
+            from test_gpu_tensor_parallel import D, HEADS, KV_HEADS, _inputs, _layer_args
+
+            batch = _inputs()
+            qs, ks = tp.kv_head_shard(HEADS, KV_HEADS, rank, world)
+            w_o = tp.o_proj_shard(batch[8], HEADS, D, rank, world, KV_HEADS).to(dev)
+            args = _layer_args(dev, qs, ks, batch)
+            red = tp.PeerAllReduce(args[0].shape[0] * w_o.shape[1], torch.bfloat16, timeout_s=5.0)
+            peer = tp.KVHeadParallelAttention(w_o=w_o, reducer=red)(*args).clone()
+            args = _layer_args(dev, qs, ks, batch)             # fresh pools: the append above wrote them
+            nccl = tp.KVHeadParallelAttention(w_o=w_o)(*args)
+            torch.cuda.synchronize(dev)
+            red.check()
+            red.close()
+            dist.barrier()
+            np.save(os.path.join(out_dir, f"peer{rank}.npy"), peer.float().cpu().numpy())
+            np.save(os.path.join(out_dir, f"nccl{rank}.npy"), nccl.float().cpu().numpy())
+        elif mode == "timeout":
+            red = tp.PeerAllReduce(4096, torch.float32, timeout_s=0.5)
+            if rank == 0:                                  # rank 1 never joins this call
+                t = red.slot((4096,))
+                t.fill_(1.0)
+                red.all_reduce_(t)
+                torch.cuda.synchronize(dev)
+                try:
+                    red.check()
+                    result["raised"] = False
+                except RuntimeError as exc:
+                    result["raised"] = "gave up waiting" in str(exc)
+                x = torch.ones(8, device=dev) * 3           # the context still works
+                result["usable"] = float(x.sum().item()) == 24.0
+            dist.barrier()
+            red.close()
+            dist.barrier()
+        Path(out_dir, f"rank{rank}.json").write_text(json.dumps(result))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(tmp_path, mode: str) -> list[dict]:
+    ctx = torch.multiprocessing.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert not p.is_alive() and p.exitcode == 0, f"rank exit code {p.exitcode}"
+    return [json.loads(Path(tmp_path, f"rank{r}.json").read_text()) for r in range(2)]
+
+
+@needs_two
+def test_peer_allreduce_is_the_rank_order_float32_sum(tmp_path):
+    res = _spawn(tmp_path, "sum")
+    for r in range(2):
+        assert res[r] and all(res[r].values()), res[r]
+    for f in sorted(tmp_path.glob("r0-*.npy")):
+        np.testing.assert_array_equal(np.load(f), np.load(tmp_path / f.name.replace("r0-", "r1-")))
+
+
+@needs_two
+def test_tensor_parallel_layer_through_peer_allreduce_matches_nccl(tmp_path):
+    _spawn(tmp_path, "layer")
+    for r in range(2):
+        np.testing.assert_allclose(np.load(tmp_path / f"peer{r}.npy"), np.load(tmp_path / f"nccl{r}.npy"),
+                                   atol=2e-2, rtol=2e-2)
+    np.testing.assert_array_equal(np.load(tmp_path / "peer0.npy"), np.load(tmp_path / "peer1.npy"))
+
+
+@needs_two
+def test_missing_peer_times_out_with_an_error(tmp_path):
+    res = _spawn(tmp_path, "timeout")
+    assert res[0] == {"raised": True, "usable": True}
