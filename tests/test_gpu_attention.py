@@ -232,3 +232,34 @@ def test_tensor_core_prefill_churn_shape(pkg, oracle):
     sub = compact_subbatch(q, kp, vp, bt, cl, ql, lengths, pick, 16)
     ref = oracle.paged_attention_gather(*sub, 128 ** -0.5, "bf16")
     _close(out[subset_rows(lengths, pick)], ref, "bf16")
+
+
+def test_shared_prefix_blocks_match_oracle(pkg, oracle):
+    """BASELINE config 4's structure: every block table starts with the same 8 physical
+    blocks (a refcounted 128-token system prefix); prefix-hit prefills (query = the
+    unique suffix, shorter than the context) and decodes read those blocks concurrently
+    in one call, on the tcgen05 prefill and tensor-pipe decode kernels."""
+    g = torch.Generator().manual_seed(31)
+    bs, heads, kv_heads, d = 16, 32, 8, 128
+    suffixes = [37, 200, 512, 16, 1, 1, 1, 1]      # four prefix-hit prefills, four decodes
+    ctx = [128 + s + (40 if q == 1 else 0) for s, q in zip([37, 200, 512, 16, 90, 300, 5, 0], suffixes)]
+    need = [-(-c // bs) for c in ctx]
+    nb = 8 + sum(n - 8 for n in need) + 4
+    perm = torch.randperm(nb, generator=g)
+    tables = torch.zeros(len(ctx), max(need), dtype=torch.long)
+    off = 8
+    for i, n in enumerate(need):
+        tables[i, :8] = perm[:8]                       # the shared prefix blocks
+        tables[i, 8:n] = perm[off:off + n - 8]
+        off += n - 8
+    kp = torch.randn(nb, bs, kv_heads, d, generator=g).to(torch.bfloat16)
+    vp = torch.randn(nb, bs, kv_heads, d, generator=g).to(torch.bfloat16)
+    q = torch.randn(sum(suffixes), heads, d, generator=g).to(torch.bfloat16)
+    cl = torch.tensor(ctx, dtype=torch.long)
+    ql = torch.tensor(suffixes, dtype=torch.long)
+    out = _run(pkg, q, kp, vp, tables, cl, ql, d ** -0.5).float().cpu().numpy()
+    assert {"prefill_tc", "decode_mma"} <= pkg._lib.last_launches()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), tables.numpy(),
+                                        cl.numpy(), ql.numpy(), d ** -0.5, "bf16")
+    _close(out, ref, "bf16", "shared prefix blocks")
+    assert pkg.read_device_error() == 0
