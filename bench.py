@@ -625,17 +625,53 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
                 host["out"][:tokens].copy_(out, non_blocking=True)
                 moved[1] += out.numel() * 2
 
+    graph = None
+    if args.graphs:                 # the decode pass as one captured CUDA graph per step
+        import importlib
+
+        graphs = importlib.import_module(f"{pkg.__name__}.graphs")
+        graph = graphs.DecodeStepGraph(k_pools, v_pools, Hq, D ** -0.5, B, wl.tables.shape[1], device=dev)
+        for l in range(L):
+            graph.q[l].copy_(dec.q[l])
+            graph.k_new[l].copy_(dec.k[l])
+            graph.v_new[l].copy_(dec.v[l])
+
+    def decode_graph(s, marks=None, src=None):
+        graph.set_step(wl.decode_ctx[s], wl.tables)
+        if src is not None:
+            for dst, h in zip((graph.q, graph.k_new, graph.v_new), src):
+                for l in range(L):
+                    dst[l].copy_(h[:B], non_blocking=True)
+                moved[0] += L * h[:B].numel() * 2
+            moved[0] += 4 * graph.words
+        if marks is not None:
+            marks[0][0].record(stream)
+        if graph.graph is None:
+            graph.capture()
+        else:
+            graph.replay()
+        if marks is not None:
+            marks[0][1].record(stream)
+        launches[0] += L * 3
+        if src is not None:
+            for l in range(L):
+                host["out"][:B].copy_(graph.out[l], non_blocking=True)
+            moved[1] += L * B * Hq * D * 2
+
     def step(s, md=None, mp=None, e2e=False):
         if e2e:                     # plan and upload this step's metadata inside the timed region
-            dm = plan_decode(s)
+            dm = plan_decode(s) if graph is None else None
             pm = plan_prefill(s)
-            moved[0] += 4 * (int(dm.plan.words) + (int(pm.plan.words) if pm is not None else 0))
-            dm, pm = dm.upload(dev), (pm.upload(dev) if pm is not None else None)
+            moved[0] += 4 * ((int(dm.plan.words) if dm is not None else 0) + (int(pm.plan.words) if pm is not None else 0))
+            dm, pm = (dm.upload(dev) if dm is not None else None), (pm.upload(dev) if pm is not None else None)
         else:
             dm, pm = metas[s]
         if pm is not None:
             run_pass(pm, bts_pre[s], pre, pm.num_tokens, mp, host["pre"] if e2e else None)
-        run_pass(dm, bt, dec, B, md, host["dec"] if e2e else None)
+        if graph is not None:
+            decode_graph(s, md, host["dec"] if e2e else None)
+        else:
+            run_pass(dm, bt, dec, B, md, host["dec"] if e2e else None)
 
     clocks = ClockSampler(dev.index)
     with clocks:
@@ -672,7 +708,8 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
     timed = [args.warmup + k for k in range(args.steps)]
     elapsed = t0.elapsed_time(t1)
     e2e_ms = e0.elapsed_time(e1)
-    dec_ms = float(np.mean([m[0].elapsed_time(m[1]) for mk in md for m in mk]))
+    dec_ms = (float(np.mean([m[0].elapsed_time(m[1]) for mk in md for m in mk])) if graph is None else
+              float(np.mean([mk[0][0].elapsed_time(mk[0][1]) for mk in md])) / L)   # a replay covers all layers
     pre_list = [m[0].elapsed_time(m[1]) for k, mk in enumerate(mp) if metas[timed[k]][1] is not None for m in mk]
     pre_ms = float(np.sum(pre_list)) / L / args.steps if pre_list else 0.0   # per layer, averaged over steps
     times = torch.tensor([elapsed, dec_ms, pre_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -699,7 +736,9 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
                    "layers": L, "admitted_per_step": admitted, "seq_len": "ragged (prefix 128 + suffix + output)",
                    "l2": "decode K/V of the whole batch per layer exceeds L2 except the shared prefix blocks, "
                          "which every sequence re-reads (L2 hits); no flush",
-                   "parallelism": f"replicas x{world} (request-level data parallel, no collectives)"},
+                   "parallelism": f"replicas x{world} (request-level data parallel, no collectives)",
+                   "decode_pass": "one CUDA graph per step (captured append + attention for all layers)"
+                   if graph is not None else "eager launches"},
         "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                      "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "peak_source": f"{peak_kind} HBM copy",
                      "traffic": None, "kernel": "decode paged attention per layer (tensor-pipe MMA + combine); "
@@ -1117,6 +1156,8 @@ def main() -> None:
     ap.add_argument("--cpu-sample-seqs", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graphs", action="store_true",
+                    help="config4: run the decode pass as a captured CUDA graph per step")
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="config5 at N>1: the o_proj all-reduce over NVLink peer memory (default) or NCCL")
     args = ap.parse_args()

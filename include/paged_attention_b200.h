@@ -126,6 +126,24 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
                      int32_t num_kv_heads, int32_t sm_count, int32_t prefill_tile_tokens,
                      int32_t* meta_out, int64_t meta_capacity, pa_step_plan* plan);
 
+/*
+ * A decode-step plan padded to a fixed shape, so that every launch parameter of
+ * pa_reshape_and_cache / pa_paged_attention_fwd stays the same from step to step and a
+ * CUDA graph captured once can be replayed with each step's metadata copied into the
+ * same device buffer.  No reference counterpart (the reference launches per call);
+ * the arrays are those of pa_plan_step for an all-decode batch (every query_len 1,
+ * num_tokens = num_seqs), with the split size fixed to split_blocks, block tables
+ * width_cap wide, and the decode-item and combine lists padded with null entries
+ * (sequence -1, skipped by the kernels) to items_cap and combine_cap.  A step that does
+ * not fit returns PA_ERR_BUFFER_TOO_SMALL ("bucket: ..."); the caller then picks a larger
+ * bucket.  With meta_out NULL it only fills *plan (plan->words sizes the buffer).
+ */
+int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, const int64_t* block_tables,
+                              int64_t table_row_stride, int32_t table_cols, int64_t pool_num_blocks,
+                              int32_t block_size, int32_t num_kv_heads, int32_t split_blocks, int32_t width_cap,
+                              int32_t items_cap, int32_t combine_cap, int32_t* meta_out, int64_t meta_capacity,
+                              pa_step_plan* plan);
+
 /* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape. */
 uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim);
 

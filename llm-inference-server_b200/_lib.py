@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class StepPlan(ctypes.Structure):
@@ -105,6 +105,8 @@ _SIGNATURES = {
     "pa_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
     "pa_ipc_open": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),
     "pa_ipc_close": (c_int32, [c_void_p, c_int64]),
+    "pa_plan_decode_padded": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int64, c_int32, c_int32,
+                                        c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, POINTER(StepPlan)]),
 }
 
 _lib = None
@@ -145,6 +147,10 @@ def last_launches() -> set[str]:
     return {n for bit, n in names.items() if mask & bit}
 
 
+class BucketOverflow(ValueError):
+    """A step does not fit the fixed shape of a padded (CUDA-graph) plan."""
+
+
 def check(rc: int) -> None:
     """Map a C return code to the reference's exception types."""
     if rc == PA_OK:
@@ -154,4 +160,6 @@ def check(rc: int) -> None:
         raise ValueError(msg)
     if rc == PA_ERR_UNSUPPORTED:
         raise NotImplementedError(f"ATTENTION=cuda: {msg}")
+    if rc == PA_ERR_BUFFER_TOO_SMALL and msg.startswith("bucket"):
+        raise BucketOverflow(msg)
     raise RuntimeError(msg)

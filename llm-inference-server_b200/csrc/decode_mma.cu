@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps)
   // each pool block they read reach DRAM close together.
   const int4 item = p.items[blockIdx.x / p.num_kv_heads];
   const int seq = item.x, split = item.y, part = item.z, nsplit = item.w;
+  if (seq < 0) return;  // padding of a bucketed (CUDA-graph) plan
   const int kvh = blockIdx.x % p.num_kv_heads;
   const int ctx = p.ctx_lens[seq];
   const int tok = p.cu_q[seq];

@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(32 * kDecodeWarps)
   // each pool block they read reach DRAM close together.
   const int4 item = p.items[blockIdx.x / p.num_kv_heads];
   const int seq = item.x, split = item.y, part = item.z, nsplit = item.w;
+  if (seq < 0) return;  // padding of a bucketed (CUDA-graph) plan
   const int kvh = blockIdx.x % p.num_kv_heads;
   const int ctx = p.ctx_lens[seq];
   const int tok = p.cu_q[seq];
@@ -298,6 +299,7 @@ __global__ void __launch_bounds__(32 * kDecodeWarps)
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const CombineParams p) {
   const int4 c = p.combine[blockIdx.x];
+  if (c.x < 0) return;  // padding of a bucketed (CUDA-graph) plan
   const int tok = c.y, first = c.z, ns = c.w;
   const int h = blockIdx.y;
   float M = -INFINITY;

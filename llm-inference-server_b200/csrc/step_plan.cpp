@@ -53,7 +53,7 @@ static int choose_split(const std::vector<int>& decode_nblk, int num_kv_heads, i
 
 extern "C" {
 
-int32_t pa_abi_version(void) { return 3; }
+int32_t pa_abi_version(void) { return 4; }
 
 const char* pa_last_error(void) { return pa::last_error(); }
 
@@ -65,11 +65,21 @@ int64_t pa_plan_words_bound(int32_t num_seqs, int32_t num_tokens, int32_t max_bl
   return B * W + 3 * B + 1 + 3 * T + 4 * B * W + 4 * B + 2 * T + 64;
 }
 
-int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int32_t num_seqs,
-                     const int64_t* block_tables, int64_t table_row_stride, int32_t table_cols,
-                     int32_t num_tokens, int64_t pool_num_blocks, int32_t block_size,
-                     int32_t num_kv_heads, int32_t sm_count, int32_t prefill_tile_tokens,
-                     int32_t* meta_out, int64_t meta_capacity, pa_step_plan* plan) {
+}  // extern "C"
+
+namespace pa {
+
+// Fixed shape of a padded decode plan (a CUDA-graph bucket): split size, table width and
+// the capacities the decode-item and combine lists are padded to.
+struct PlanCaps {
+  int32_t split_blocks, width, items, combine;
+};
+
+static int32_t plan_impl(const int64_t* context_lens, const int64_t* query_lens, int32_t num_seqs,
+                         const int64_t* block_tables, int64_t table_row_stride, int32_t table_cols,
+                         int32_t num_tokens, int64_t pool_num_blocks, int32_t block_size, int32_t num_kv_heads,
+                         int32_t sm_count, int32_t prefill_tile_tokens, int32_t* meta_out, int64_t meta_capacity,
+                         pa_step_plan* plan, const PlanCaps* caps) {
   using pa::fail;
   if (!plan) return fail(PA_ERR_INVALID_ARGUMENT, "plan must not be NULL");
   std::memset(plan, 0, sizeof(*plan));
@@ -116,6 +126,18 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
   }
   if (pool_num_blocks * int64_t(block_size) > (int64_t(1) << 31) - 1)
     return fail(PA_ERR_UNSUPPORTED, "pool has more than 2^31 slots");
+  if (caps) {
+    if (num_tokens != num_seqs)
+      return fail(PA_ERR_UNSUPPORTED, "a padded plan is for decode steps (every query_len 1)");
+    for (int i = 0; i < num_seqs; ++i)
+      if (query_lens[i] != 1) return fail(PA_ERR_UNSUPPORTED, "a padded plan is for decode steps (every query_len 1)");
+    if (caps->split_blocks <= 0 || caps->width <= 0 || caps->items < 0 || caps->combine < 0)
+      return fail(PA_ERR_INVALID_ARGUMENT, "bad padded-plan capacities");
+    if (width > caps->width)
+      return fail(PA_ERR_BUFFER_TOO_SMALL, "bucket: a context needs %d blocks, the bucket's tables hold %d", width,
+                  caps->width);
+    width = caps->width;
+  }
 
   // ---- split-K decode work list
   std::vector<int> decode_seqs, decode_nblk;
@@ -129,12 +151,20 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
       n_prefill_tok += int(query_lens[i]);
     }
   }
-  const int sb = pa::choose_split(decode_nblk, num_kv_heads, sm_count);
+  const int sb = caps ? caps->split_blocks : pa::choose_split(decode_nblk, num_kv_heads, sm_count);
   int64_t n_items = 0, n_combine = 0;
   for (int n : decode_nblk) {
     const int ns = (n + sb - 1) / sb;
     n_items += ns;
     if (ns > 1) ++n_combine;
+  }
+  const int64_t real_items = n_items, real_combine = n_combine;
+  if (caps) {
+    if (n_items > caps->items || n_combine > caps->combine)
+      return fail(PA_ERR_BUFFER_TOO_SMALL, "bucket: %lld work items / %lld combines, the bucket holds %d / %d",
+                  (long long)n_items, (long long)n_combine, caps->items, caps->combine);
+    n_items = caps->items;
+    n_combine = caps->combine;
   }
   int64_t n_tiles = 0;
   if (prefill_tile_tokens > 0)
@@ -243,6 +273,13 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
       items[4 * w + 3] = it.nsplit;
       ++w;
     }
+  // Padding of a bucketed plan: null items and combines (sequence -1) the kernels skip.
+  for (; w < n_items; ++w) {
+    items[4 * w + 0] = -1;
+    items[4 * w + 2] = -1;
+  }
+  for (int64_t c = real_combine; c < n_combine; ++c) comb[4 * c + 0] = -1;
+  (void)real_items;
 
   // Prefill tiles in launch order, heaviest first: a tile's work is the causal key range
   // of its last token, so the grid's tail is made of the tiles with the fewest keys
@@ -265,6 +302,31 @@ int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int
     }
   }
   return PA_OK;
+}
+
+}  // namespace pa
+
+extern "C" {
+
+int32_t pa_plan_step(const int64_t* context_lens, const int64_t* query_lens, int32_t num_seqs,
+                     const int64_t* block_tables, int64_t table_row_stride, int32_t table_cols,
+                     int32_t num_tokens, int64_t pool_num_blocks, int32_t block_size,
+                     int32_t num_kv_heads, int32_t sm_count, int32_t prefill_tile_tokens,
+                     int32_t* meta_out, int64_t meta_capacity, pa_step_plan* plan) {
+  return pa::plan_impl(context_lens, query_lens, num_seqs, block_tables, table_row_stride, table_cols, num_tokens,
+                       pool_num_blocks, block_size, num_kv_heads, sm_count, prefill_tile_tokens, meta_out,
+                       meta_capacity, plan, nullptr);
+}
+
+int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, const int64_t* block_tables,
+                              int64_t table_row_stride, int32_t table_cols, int64_t pool_num_blocks,
+                              int32_t block_size, int32_t num_kv_heads, int32_t split_blocks, int32_t width_cap,
+                              int32_t items_cap, int32_t combine_cap, int32_t* meta_out, int64_t meta_capacity,
+                              pa_step_plan* plan) {
+  std::vector<int64_t> ones(size_t(std::max(num_seqs, 0)), 1);
+  const pa::PlanCaps caps{split_blocks, width_cap, items_cap, combine_cap};
+  return pa::plan_impl(context_lens, ones.data(), num_seqs, block_tables, table_row_stride, table_cols, num_seqs,
+                       pool_num_blocks, block_size, num_kv_heads, 0, 0, meta_out, meta_capacity, plan, &caps);
 }
 
 }  // extern "C"

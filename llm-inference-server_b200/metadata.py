@@ -95,6 +95,32 @@ class StepMetadata:
         return meta
 
     @classmethod
+    def plan_decode_padded(cls, context_lens, block_tables, *, pool_num_blocks: int, block_size: int,
+                           num_kv_heads: int, split_blocks: int, width: int, items: int, combine: int,
+                           host: np.ndarray | None = None) -> "StepMetadata":
+        """An all-decode step planned to a fixed shape (a CUDA-graph bucket): split size
+        ``split_blocks``, tables ``width`` wide, ``items`` decode work items and ``combine``
+        combine entries (the unused ones are null entries the kernels skip).  Writes into
+        ``host`` when given (a graph's pinned buffer).  Raises ValueError("bucket: ...")
+        when the step does not fit."""
+        lib = _lib.lib()
+        ctx = _as_i64(context_lens)
+        bt = _as_i64(block_tables)
+        if bt.ndim != 2 or ctx.shape != (bt.shape[0],):
+            raise ValueError("block_tables must be [batch, max_blocks] and context_lens [batch]")
+        plan = _lib.StepPlan()
+        args = (ctx.ctypes.data, ctx.shape[0], bt.ctypes.data, bt.shape[1], bt.shape[1], int(pool_num_blocks),
+                int(block_size), int(num_kv_heads), int(split_blocks), int(width), int(items), int(combine))
+        _lib.check(lib.pa_plan_decode_padded(*args, None, 0, ctypes.byref(plan)))
+        words = max(int(plan.words), 1)
+        if host is None:
+            host = np.empty(words, dtype=np.int32)
+        elif host.size < words:
+            raise ValueError(f"host buffer holds {host.size} words, the plan needs {words}")
+        _lib.check(lib.pa_plan_decode_padded(*args, host.ctypes.data, host.size, ctypes.byref(plan)))
+        return cls(plan, host, pool_num_blocks)
+
+    @classmethod
     def build(cls, context_lens, query_lens, block_tables, *, num_tokens: int, pool_num_blocks: int,
               block_size: int, num_kv_heads: int, device, prefill_tile_tokens: int = 0) -> "StepMetadata":
         """Plan on the host and upload to ``device`` with one asynchronous copy."""

@@ -20,7 +20,7 @@ REFERENCE_SIGNATURE = ["query", "k_pool", "v_pool", "block_tables", "context_len
 def test_library_exports_every_declared_symbol(pkg):
     lib = pkg._lib.lib()
     declared = pkg._lib.declared_symbols()
-    assert len(declared) == 17
+    assert len(declared) == 18
     for name in declared:
         assert hasattr(lib, name), name
     dyn = subprocess.run(["nm", "-D", "--defined-only", str(pkg._lib.LIB_PATH)], capture_output=True,
@@ -132,6 +132,41 @@ def test_split_size_fills_the_gpu(pkg):
     m = _plan(pkg, ctx, np.ones(256, np.int64), tables, num_blocks=1, bs=16, kv_heads=8)
     assert m.plan.num_decode_items * 8 >= 148 * 8
     assert 1 <= m.plan.split_blocks <= 32
+
+
+def test_padded_decode_plan_keeps_the_real_entries(pkg):
+    """A CUDA-graph bucket's plan: the same tables, lengths, slots, work items and
+    combines as the ordinary plan at the same split size, padded with null entries, and
+    fixed counts and offsets however the contexts move inside the bucket."""
+    rng = np.random.default_rng(4)
+    ctx = rng.integers(1, 600, size=24).astype(np.int64)
+    need = -(-ctx // 16)
+    tables = np.zeros((24, 64), dtype=np.int64)
+    for i, n in enumerate(need):
+        tables[i, :n] = rng.permutation(4000)[:n]
+    kw = dict(pool_num_blocks=4000, block_size=16, num_kv_heads=8)
+    base = pkg.StepMetadata.plan_host(ctx, np.ones(24, np.int64), tables, num_tokens=24, sm=1, **kw)
+    sb = int(base.plan.split_blocks)
+    pad = pkg.StepMetadata.plan_decode_padded(ctx, tables, split_blocks=sb, width=64, items=200, combine=30, **kw)
+    p, b = pad.plan, base.plan
+    assert (p.table_width, p.num_decode_items, p.num_combine_seqs, p.split_blocks) == (64, 200, 30, sb)
+    np.testing.assert_array_equal(pad.block_tables(False)[:, :b.table_width], base.block_tables(False))
+    assert not pad.block_tables(False)[:, b.table_width:].any()
+    np.testing.assert_array_equal(pad.slot_mapping(False), base.slot_mapping(False))
+    items = pad.decode_items()
+    np.testing.assert_array_equal(items[:b.num_decode_items], base.decode_items())
+    assert (items[b.num_decode_items:, 0] == -1).all()
+    comb = pad.host[p.off_combine:p.off_combine + 4 * 30].reshape(30, 4)
+    np.testing.assert_array_equal(comb[:b.num_combine_seqs],
+                                  base.host[b.off_combine:b.off_combine + 4 * b.num_combine_seqs].reshape(-1, 4))
+    assert (comb[b.num_combine_seqs:, 0] == -1).all()
+    later = pkg.StepMetadata.plan_decode_padded(ctx + 7, tables, split_blocks=sb, width=64, items=200, combine=30, **kw)
+    offs = [n for n, _ in pkg._lib.StepPlan._fields_ if n.startswith("off_") or n == "words"]
+    assert all(getattr(later.plan, n) == getattr(p, n) for n in offs)
+    with pytest.raises(ValueError, match="bucket"):
+        pkg.StepMetadata.plan_decode_padded(ctx, tables, split_blocks=sb, width=64, items=4, combine=30, **kw)
+    with pytest.raises(ValueError, match="bucket"):
+        pkg.StepMetadata.plan_decode_padded(ctx, tables, split_blocks=sb, width=8, items=200, combine=30, **kw)
 
 
 def test_seam_keeps_the_gather_signature(pkg, oracle):
