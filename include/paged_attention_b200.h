@@ -144,6 +144,11 @@ int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, con
                               int32_t items_cap, int32_t combine_cap, int32_t* meta_out, int64_t meta_capacity,
                               pa_step_plan* plan);
 
+/* (token, query-head) rows of one tensor-core prefill tile: plan prefill steps with
+ * prefill_tile_tokens = pa_prefill_tile_rows() / (num_heads / num_kv_heads) so their
+ * rows take the tcgen05 kernel. */
+int32_t pa_prefill_tile_rows(void);
+
 /* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape. */
 uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim);
 

@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class StepPlan(ctypes.Structure):
@@ -76,6 +76,7 @@ class StepPlan(ctypes.Structure):
 
 _SIGNATURES = {
     "pa_abi_version": (c_int32, []),
+    "pa_prefill_tile_rows": (c_int32, []),
     "pa_last_launches": (c_int32, []),
     "pa_last_error": (c_char_p, []),
     "pa_plan_words_bound": (c_int64, [c_int32, c_int32, c_int32]),

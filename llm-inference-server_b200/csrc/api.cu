@@ -399,6 +399,8 @@ int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t nu
                     num_blocks, staging, error_word, stream, "scatter_blocks");
 }
 
+int32_t pa_prefill_tile_rows(void) { return pa::prefill_tile_rows(); }
+
 int32_t pa_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
   using namespace pa;
   if (!dev_ptr || !handle_out || !offset_out) return fail(PA_ERR_INVALID_ARGUMENT, "ipc_export: NULL pointer");
