@@ -36,7 +36,7 @@ const char* last_error() { return g_last_error.c_str(); }
 
 // Decode split size: the largest power of two (in blocks, at most kMaxSplit) that still
 // gives the grid at least kWavesTarget CTAs per SM, so long and short contexts balance.
-constexpr int kMaxSplitBlocks = 32;
+constexpr int kMaxSplitBlocks = 128;
 constexpr int kCtasPerSmTarget = 8;
 
 static int choose_split(const std::vector<int>& decode_nblk, int num_kv_heads, int sm_count) {
