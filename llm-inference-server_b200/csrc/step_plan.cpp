@@ -34,10 +34,11 @@ int32_t fail(int32_t code, const char* fmt, ...) {
 
 const char* last_error() { return g_last_error.c_str(); }
 
-// Decode split size: the largest power of two (in blocks, at most kMaxSplit) that still
-// gives the grid at least kWavesTarget CTAs per SM, so long and short contexts balance.
-constexpr int kMaxSplitBlocks = 128;
-constexpr int kCtasPerSmTarget = 8;
+// Decode split size: the largest power of two (in blocks, at most kMaxSplitBlocks) that
+// still gives the grid at least kCtasPerSmTarget CTAs per SM, so long and short contexts
+// balance while each CTA streams enough blocks to amortise its setup and its partial.
+constexpr int kMaxSplitBlocks = 256;
+constexpr int kCtasPerSmTarget = 4;
 
 static int choose_split(const std::vector<int>& decode_nblk, int num_kv_heads, int sm_count) {
   const int64_t target = int64_t(std::max(sm_count, 1)) * kCtasPerSmTarget;
