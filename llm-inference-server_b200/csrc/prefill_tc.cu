@@ -428,6 +428,10 @@ static cudaError_t launch_pf_one(const CUtensorMap& tk, const CUtensorMap& tv, c
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
+    // Largest shared-memory carveout, so the designed number of CTAs fits on every SM
+    // whatever the driver would otherwise pick for this launch.
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   dim3 grid(p.num_tiles, p.num_kv_heads), block(kPfThreads);
