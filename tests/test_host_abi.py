@@ -214,3 +214,32 @@ def test_words_bound_covers_plans(pkg):
         tables = np.zeros((b, int(need.max())), dtype=np.int64)
         m = _plan(pkg, ctx, ql, tables, num_blocks=1, bs=16, kv_heads=8, sm=148, tile=64)
         assert m.plan.words <= lib.pa_plan_words_bound(b, int(ql.sum()), int(need.max()))
+
+
+def test_multi_gpu_and_block_entry_points_reject_bad_arguments(pkg):
+    """The argument checks of the block moves, the peer all-reduce and CUDA IPC run on the
+    host before any device work (so they hold without a GPU) and name the problem."""
+    import ctypes
+
+    lib = pkg._lib.lib()
+    arr = (ctypes.c_void_p * 1)(None)
+    err = ctypes.c_int32(0)
+    with pytest.raises(ValueError, match="multiple of 16"):
+        pkg._lib.check(lib.pa_copy_blocks(arr, arr, 1, 8, 24, None, 1, ctypes.addressof(err), None))
+    with pytest.raises(ValueError, match="bad sizes"):
+        pkg._lib.check(lib.pa_gather_blocks(arr, arr, -1, 8, 32, None, 1, None, ctypes.addressof(err), None))
+    pkg._lib.check(lib.pa_scatter_blocks(arr, arr, 1, 8, 32, None, 0, None, ctypes.addressof(err), None))  # no-op
+    bases = (ctypes.c_void_p * 2)(None, None)
+    with pytest.raises(ValueError, match="rank 2 of 2"):
+        pkg._lib.check(lib.pa_peer_allreduce(bases, 2, 2, 0, 256, 64, 2, 1.0, ctypes.addressof(err), None))
+    with pytest.raises(ValueError, match="at most 8"):
+        pkg._lib.check(lib.pa_peer_allreduce(bases, 9, 0, 0, 256, 64, 2, 1.0, ctypes.addressof(err), None))
+    with pytest.raises(NotImplementedError, match="16-byte vectors"):
+        pkg._lib.check(lib.pa_peer_allreduce(bases, 2, 0, 0, 256, 3, 2, 1.0, ctypes.addressof(err), None))
+    with pytest.raises(ValueError, match="timeout"):
+        pkg._lib.check(lib.pa_peer_allreduce(bases, 2, 0, 0, 256, 64, 2, 0.0, ctypes.addressof(err), None))
+    with pytest.raises(ValueError, match="NULL"):
+        pkg._lib.check(lib.pa_ipc_export(None, None, None))
+    with pytest.raises(ValueError):
+        pkg._lib.check(lib.pa_ipc_open(None, 0, None))
+    assert pkg.metadata.prefill_tile_rows() == lib.pa_prefill_tile_rows() > 0
