@@ -23,7 +23,9 @@ Decode contexts grow by one token per step.  Tokens generated per step: 256 + 13
   before the timed region), CUDA events on the launching stream, max over ranks.
 * ``e2e``    the same through the public API with HOST buffers: every step plans and
   uploads its metadata, copies each layer's q / new K / new V from pinned host memory
-  and reads each layer's attention output back.
+  and reads each layer's attention output back.  The uploads and read-backs run on two
+  copy streams into double-buffered device slots, overlapped with the neighbouring
+  layers' compute (PCIe carries both directions at once), as a serving loop would.
 * ``roofline``  the decode attention launches (the dominant kernel): algorithmic bytes
   (K+V of every context once, q and out, block ids, lengths) over their CUDA-event time,
   against the measured HBM copy peak.  ``prefill_roofline``: the prefill attention
@@ -39,6 +41,7 @@ the reference algorithm's CPU port instead (rank 0 only).
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -138,6 +141,27 @@ def _measured_peaks() -> tuple[float, float, str]:
         except Exception:
             pass
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback"
+
+
+class QuietHost:
+    """Keeps Python's cyclic garbage collector out of a timed region: everything alive is
+    collected once and frozen (no later collection walks it) and automatic collection is
+    off until the region ends.  The enqueue loops here run only ~100 ms ahead of the GPU,
+    and a full collection in a process with torch loaded takes about that long, so one
+    would idle the GPU inside a single launch's event pair."""
+
+    def __enter__(self):
+        gc.collect()
+        gc.freeze()
+        self._enabled = gc.isenabled()
+        gc.disable()
+        return self
+
+    def __exit__(self, *exc):
+        if self._enabled:
+            gc.enable()
+        gc.unfreeze()
+        return False
 
 
 class ClockSampler:
@@ -413,7 +437,7 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
             torch.distributed.barrier()
 
     clocks = ClockSampler(dev.index)
-    with clocks:
+    with clocks, QuietHost():
         for s in range(args.warmup):
             step(metas[s])
         barrier()
@@ -677,7 +701,7 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
             run_pass(dm, bt, dec, B, md, host["dec"] if e2e else None)
 
     clocks = ClockSampler(dev.index)
-    with clocks:
+    with clocks, QuietHost():
         for s in range(args.warmup):
             step(s)
         if world > 1:
@@ -867,7 +891,7 @@ def run_engine(args, rank: int, world: int, local_rank: int) -> None:
     reqs = _c1_requests(200, args.seed + rank)
     results = {}
     clocks = ClockSampler(dev.index)
-    with clocks:
+    with clocks, QuietHost():
         _serve(ex, _c1_requests(8, 99), 4, 2048)          # warm-up: kernels, cuBLAS, allocator
         torch.cuda.synchronize(dev)
         for conc in sorted({4, args.batch}):
@@ -1002,7 +1026,7 @@ def run_blocks(args, rank: int, world: int, local_rank: int) -> None:
             marks[3].record(stream)
 
     clocks = ClockSampler(dev.index)
-    with clocks:
+    with clocks, QuietHost():
         for s in range(args.warmup):
             step(s)
         torch.cuda.synchronize(dev)
@@ -1091,6 +1115,7 @@ class _Pass:
         self.q = [torch.randn(tokens, Hq, D, generator=g, device=dev).to(dtype) for _ in range(L)]
         self.k = [torch.randn(tokens, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
         self.v = [torch.randn(tokens, Hkv, D, generator=g, device=dev).to(dtype) for _ in range(L)]
+        self.free = [None, None]   # e2e: event after the last read of each device input slot
 
 
 def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
@@ -1144,18 +1169,12 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             torch.distributed.barrier()
 
-    def run_pass(meta, bt, inp, tokens, ev=None, q_src=None, kv_src=None, out_host=None):
+    def run_pass(meta, bt, inp, tokens, ev=None):
         """Per layer: fused append of the pass's new tokens, then attention."""
         slots = meta.slot_mapping()
         bt = pkg.attach(bt, meta)
         for layer in range(L):
-            if q_src is not None:   # e2e: this layer's inputs come from pinned host memory
-                inp.q[0][:tokens].copy_(q_src[0][:tokens], non_blocking=True)
-                inp.k[0][:tokens].copy_(kv_src[0][:tokens], non_blocking=True)
-                inp.v[0][:tokens].copy_(kv_src[1][:tokens], non_blocking=True)
-                q, k, v = inp.q[0][:tokens], inp.k[0][:tokens], inp.v[0][:tokens]
-            else:
-                q, k, v = inp.q[layer][:tokens], inp.k[layer][:tokens], inp.v[layer][:tokens]
+            q, k, v = inp.q[layer][:tokens], inp.k[layer][:tokens], inp.v[layer][:tokens]
             pkg.reshape_and_cache(k, v, k_pools[layer], v_pools[layer], slots)
             if ev is not None:
                 ev[layer][0].record(stream)
@@ -1163,8 +1182,49 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
             if ev is not None:
                 ev[layer][1].record(stream)
             launches[0] += 1 + bin(lib.pa_last_launches()).count("1")   # append + attention kernels
-            if out_host is not None:
+
+    # e2e copy streams: PCIe is full duplex, so layer l+1's inputs travel up (h2d) and
+    # layer l-1's output travels down (d2h) while layer l computes; a step then costs
+    # about the larger of its upload, its read-back and its compute, not their sum.
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    nslot = min(2, L)                   # device input slots per pass (double buffering)
+
+    def run_pass_host(meta, bt, inp, tokens, q_src, kv_src, out_host):
+        """run_pass with each layer's q / new K / new V copied from pinned host memory
+        into a device slot and each layer's attention output read back to the host."""
+        slots = meta.slot_mapping()
+        bt = pkg.attach(bt, meta)
+        loaded = [torch.cuda.Event() for _ in range(L)]
+
+        def load(layer: int):
+            s = layer % nslot
+            if inp.free[s] is None:     # first use of the slot: after everything before it
+                h2d.wait_stream(stream)
+            else:                       # after the last attention that read this slot
+                h2d.wait_event(inp.free[s])
+            with torch.cuda.stream(h2d):
+                inp.q[s][:tokens].copy_(q_src[0][:tokens], non_blocking=True)
+                inp.k[s][:tokens].copy_(kv_src[0][:tokens], non_blocking=True)
+                inp.v[s][:tokens].copy_(kv_src[1][:tokens], non_blocking=True)
+            loaded[layer].record(h2d)
+
+        for layer in range(nslot):
+            load(layer)
+        for layer in range(L):
+            s = layer % nslot
+            stream.wait_event(loaded[layer])
+            q, k, v = inp.q[s][:tokens], inp.k[s][:tokens], inp.v[s][:tokens]
+            pkg.reshape_and_cache(k, v, k_pools[layer], v_pools[layer], slots)
+            out = pkg.paged_attention_cuda(q, k_pools[layer], v_pools[layer], bt, dummy_lens, dummy_lens, scale)
+            done = torch.cuda.Event()
+            done.record(stream)
+            inp.free[s] = done
+            if layer + nslot < L:
+                load(layer + nslot)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
                 out_host[:tokens].copy_(out, non_blocking=True)
+            out.record_stream(d2h)      # the allocator keeps `out` until its read-back ends
 
     def events():
         return [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
@@ -1176,7 +1236,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         run_pass(metas_d[s], bt_dec, dec, B, ev_d)
 
     clocks = ClockSampler(dev.index)
-    with clocks:
+    with clocks, QuietHost():
         # ---- value: device-resident inputs
         for s in range(args.warmup):
             device_step(s)
@@ -1187,9 +1247,11 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         ev_d = [events() for _ in range(args.steps)]
         ev_p = [events() for _ in range(args.steps)]
         start.record(stream)
+        t_host = time.perf_counter()
         for k in range(args.steps):
             device_step(args.warmup + k, ev_d[k], ev_p[k])
         end.record(stream)
+        host_enqueue_ms = (time.perf_counter() - t_host) * 1e3
         torch.cuda.synchronize(dev)
         barrier()
         gpu_launches = launches[0]
@@ -1212,11 +1274,11 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
             if wl.n_churn:
                 mp = plan_prefill(s)
                 tp = mp.num_tokens
-                run_pass(mp, bt_pre, pre, tp, q_src=q_host_p, kv_src=kv_host_p, out_host=out_host_p)
+                run_pass_host(mp, bt_pre, pre, tp, q_host_p, kv_host_p, out_host_p)
                 h2d += int(mp.plan.words) * 4 + L * tp * (Hq + 2 * Hkv) * D * elem
                 d2h += L * tp * Hq * D * elem
             md = plan_decode(s)
-            run_pass(md, bt_dec, dec, B, q_src=q_host_d, kv_src=kv_host_d, out_host=out_host_d)
+            run_pass_host(md, bt_dec, dec, B, q_host_d, kv_host_d, out_host_d)
             h2d += int(md.plan.words) * 4 + L * B * (Hq + 2 * Hkv) * D * elem
             d2h += L * B * Hq * D * elem
             h2d_bytes.append(h2d)
@@ -1232,6 +1294,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         e_start.record(stream)
         for k in range(args.steps):
             e2e_step(args.warmup + k)
+        stream.wait_stream(d2h)            # the last read-back is inside the timed region
         e_end.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
@@ -1270,6 +1333,18 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         cpu = {"value": args.cpu_sample_seqs / (float(np.mean(reps)) * L), "unit": "tok/s", "cores": _blas_threads(),
                "kind": "port", "sample": _cpu_sample_text(wl, args.cpu_sample_seqs, ctx, len(reps))}
 
+    # rank 0's per-launch spread (CUDA events per layer): shows a bimodal launch population
+    def pct(xs, digits):
+        return [round(float(x), digits) for x in (min(xs), *np.percentile(xs, [10, 50, 90]), max(xs))]
+
+    spread = {"decode_ms_min_p10_p50_p90_max": pct(dec_ms, 4), "prefill_tflops_min_p10_p50_p90_max": None}
+    if wl.n_churn:
+        rates = [wl.prefill_flops(timed[i // L]) / (t / 1e3) / 1e12 for i, t in enumerate(pre_ms)]
+        spread["prefill_tflops_min_p10_p50_p90_max"] = pct(rates, 1)
+        slow = [(i // L, i % L, round(pre_ms[i], 3)) for i, r in enumerate(rates) if r < 0.5 * float(np.median(rates))]
+        spread["prefill_slow_launches_step_layer_ms"] = slow[:8]
+    spread["host_enqueue_ms"] = round(host_enqueue_ms, 2)
+
     source = "MEASURED_PEAKS.json" if peak_kind == "measured" else "fallback"
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -1288,6 +1363,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
             "kernel": "prefill paged attention per layer (tcgen05 varlen prefill)",
             "causal_flops_per_launch": pre_flops, "avg_launch_ms": pre_avg_ms,
             "prompt_tokens_per_step": float(np.mean([wl.prompt_lens(s).sum() for s in timed]))},
+        "launch_spread": spread,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(np.mean(h2d_bytes)),
                 "d2h_bytes_per_step": int(np.mean(d2h_bytes)), "ms_per_step": e2e_ms / args.steps},
