@@ -1248,8 +1248,11 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         ev_p = [events() for _ in range(args.steps)]
         start.record(stream)
         t_host = time.perf_counter()
+        host_step_ms = []
         for k in range(args.steps):
+            t0 = time.perf_counter()
             device_step(args.warmup + k, ev_d[k], ev_p[k])
+            host_step_ms.append((time.perf_counter() - t0) * 1e3)
         end.record(stream)
         host_enqueue_ms = (time.perf_counter() - t_host) * 1e3
         torch.cuda.synchronize(dev)
@@ -1343,7 +1346,10 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         spread["prefill_tflops_min_p10_p50_p90_max"] = pct(rates, 1)
         slow = [(i // L, i % L, round(pre_ms[i], 3)) for i, r in enumerate(rates) if r < 0.5 * float(np.median(rates))]
         spread["prefill_slow_launches_step_layer_ms"] = slow[:8]
+    # host time to enqueue the whole timed loop, and one step's enqueue right after the
+    # pre-timing synchronize (empty launch queue, so no blocking: the host's own cost)
     spread["host_enqueue_ms"] = round(host_enqueue_ms, 2)
+    spread["host_first_step_ms"] = round(host_step_ms[0], 2)
 
     source = "MEASURED_PEAKS.json" if peak_kind == "measured" else "fallback"
     line = {
