@@ -396,6 +396,11 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
     layers = [tpm.KVHeadParallelAttention(w_o=w_o[l]) for l in range(L)]
     reducer = (tpm.PeerAllReduce(B * DM, torch.bfloat16, device=dev, timeout_s=10.0)
                if world > 1 and args.allreduce == "peer" else None)
+    # --allreduce fused: the o_proj GEMM and its all-reduce in one collective (at tp1 the
+    # same kernels run the GEMM alone); weights kept K-major for it
+    fused = (tpm.FusedOProjAllReduce(B, DM, torch.bfloat16, device=dev, timeout_s=10.0)
+             if args.allreduce == "fused" else None)
+    w_nk = [w.t().contiguous() for w in w_o] if fused is not None else None
 
     def step(meta, marks=None, host=None):
         slots = meta.slot_mapping()
@@ -417,13 +422,17 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
             if marks is not None:
                 marks[l][1].record(stream)
             a2 = attn.reshape(B, -1)
-            if reducer is not None:   # the GEMM writes into the peer-mapped slot
+            if fused is not None:      # GEMM + all-reduce together (timed as the o_proj span)
+                partial = fused(a2, w_nk[l])
+            elif reducer is not None:  # the GEMM writes into the peer-mapped slot
                 partial = torch.matmul(a2, layers[l].w_o, out=reducer.slot((B, DM)))
             else:
                 partial = a2 @ layers[l].w_o
             if marks is not None:
                 marks[l][2].record(stream)
-            if reducer is not None:
+            if fused is not None:
+                pass
+            elif reducer is not None:
                 reducer.all_reduce_(partial)
             elif world > 1:
                 torch.distributed.all_reduce(partial)
@@ -492,6 +501,9 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
     hbm_peak, bf16_peak, peak_kind = _measured_peaks()
     achieved = attn_bytes / (attn_ms / 1e3) / 1e9
     ar_bytes = B * DM * 2
+    backend = ("fused with the o_proj GEMM (pa_oproj_allreduce: pushes from the GEMM epilogue over NVLink)"
+               if fused is not None else "NCCL" if reducer is None else
+               "peer memory (pa_peer_allreduce: two-shot over NVLink, GEMM output written into the peer-mapped slot)")
     line = {
         "metric": METRIC, "value": B * args.steps / (elapsed / 1e3), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
@@ -505,23 +517,27 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
                    "seq_len": "ragged (mean 8192)", "physical_layer_pools": P,
                    "l2": f"each layer call streams {per_layer / 1e9:.2f} GB of KV (>> 126 MB L2); {L} layer calls "
                          f"cycle over {P} physical pools",
-                   "parallelism": (f"tp{world} (KV-head sharding; {'peer-memory' if reducer is not None else 'NCCL'} "
-                                   "all-reduce after o_proj)") if world > 1 else "tp1"},
+                   "parallelism": (f"tp{world} (KV-head sharding; {backend} all-reduce after o_proj)")
+                                  if world > 1 else "tp1"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} HBM copy", "traffic": None,
                      "kernel": "per-rank KV append + decode paged attention per layer (tensor-pipe MMA + combine)",
                      "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
         "o_proj": {"avg_ms": gemm_ms, "tflops": 2 * B * Hq * D * DM / (gemm_ms / 1e3) / 1e12,
-                   "peak_tflops": bf16_peak, "kernel": "torch bf16 matmul (cuBLAS)"},
-        "all_reduce": None if world == 1 else {
+                   "peak_tflops": bf16_peak,
+                   "kernel": ("pa_oproj_allreduce: tcgen05 GEMM whose epilogue stores tiles into their owners' "
+                              "staging over NVLink, then the owners' sums stored into every rank (GEMM and "
+                              "all-reduce timed together here)") if fused is not None
+                             else "torch bf16 matmul (cuBLAS)"},
+        "all_reduce": None if world == 1 or fused is not None else {
             "avg_ms": ar_ms, "bytes": ar_bytes, "bus_gbs": 2 * (world - 1) / world * ar_bytes / (ar_ms / 1e3) / 1e9,
-            "backend": "NCCL" if reducer is None else "peer memory (pa_peer_allreduce: two-shot over NVLink, "
-                                                        "GEMM output written into the peer-mapped slot)"},
+            "backend": backend},
         "cpu_baseline": None,
         "e2e": {"value": B * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": words * 4 // args.steps + L * B * (Hq + 2 * Hkv) * D * 2,
                 "d2h_bytes_per_step": B * DM * 2, "ms_per_step": e2e_ms / args.steps},
-        "gpu_launches": args.steps * L * (1 + len(attn_kernels) + (1 if reducer is not None else 0)),
+        "gpu_launches": args.steps * L * (1 + len(attn_kernels) + (1 if reducer is not None else 0)
+                                          + (2 if fused is not None else 0)),
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -1416,8 +1432,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graphs", action="store_true",
                     help="config4: run the decode pass as a captured CUDA graph per step")
-    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
-                    help="config5 at N>1: the o_proj all-reduce over NVLink peer memory (default) or NCCL")
+    ap.add_argument("--allreduce", choices=["peer", "nccl", "fused"], default="peer",
+                    help="config5: the o_proj all-reduce over NVLink peer memory (default), NCCL, or fused "
+                         "with the o_proj GEMM into one peer-memory collective")
     args = ap.parse_args()
     if args.layers is None:
         args.layers = WORKLOADS[args.workload]["layers"]

@@ -294,6 +294,34 @@ int32_t pa_peer_allreduce(void* const* bases, int32_t world, int32_t rank, int64
                           int64_t count, int32_t dtype, double timeout_s, int32_t* error_word, void* stream);
 
 /*
+ * The row-split o_proj GEMM fused with its all-reduce, over peer memory: every rank ends
+ * with out[rows, n] = sum over ranks of round(a_r . w_r^T) (each rank's product rounded to
+ * the storage dtype, then summed in float32 in rank order and rounded once).  No
+ * counterpart in the reference (no multi-GPU path): it replaces `attn @ w_o` plus
+ * torch.distributed.all_reduce in KV-head tensor parallelism.  bf16 or fp16 only.
+ *
+ *   a             this rank's [rows, k] activations (row stride a_row_stride elements,
+ *                 a multiple of 8; 16-byte aligned)
+ *   w             this rank's o_proj slice, K-major [n, k] contiguous (16-byte aligned)
+ *   k, n          k a multiple of 64; n a multiple of 128 * world
+ *   bases         HOST array of `world` device pointers: every rank's buffer (CUDA IPC),
+ *                 same layout on all ranks: a staging area of rows * n elements at
+ *                 stage_offset, the output [rows, n] at out_offset, a zero-initialised
+ *                 128-byte flag area at flags_offset (offsets 16-byte aligned)
+ *   timeout_s     bound on each wait for a peer; on expiry bit 4 of *error_word is set
+ *                 and the buffer must not be used again
+ *
+ * Two launches on `stream` (the GEMM, whose epilogue stores each output tile into the
+ * staging area of the rank owning its columns, then the owners' sums stored into every
+ * rank's output).  Every rank must make the same sequence of calls with the same rows,
+ * k, n and offsets; the output is complete on this rank when the second launch ends.
+ */
+int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, int32_t k, const void* w, int32_t n,
+                           int32_t dtype, void* const* bases, int32_t world, int32_t rank, int64_t stage_offset,
+                           int64_t out_offset, int64_t flags_offset, double timeout_s, int32_t* error_word,
+                           void* stream);
+
+/*
  * Read (and clear, when clear != 0) the device error word a workspace carries.  It is
  * set by kernels that met an out-of-range block id or slot (the host checks make this
  * unreachable for planned steps) or a pipeline wait that ran out of its iteration

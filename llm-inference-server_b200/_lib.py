@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class StepPlan(ctypes.Structure):
@@ -106,6 +106,9 @@ _SIGNATURES = {
     "pa_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
     "pa_ipc_open": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),
     "pa_ipc_close": (c_int32, [c_void_p, c_int64]),
+    "pa_oproj_allreduce": (c_int32, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int32, c_int32,
+                                     POINTER(c_void_p), c_int32, c_int32, c_int64, c_int64, c_int64, ctypes.c_double,
+                                     c_void_p, c_void_p]),
     "pa_plan_decode_padded": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int64, c_int32, c_int32,
                                         c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, POINTER(StepPlan)]),
 }

@@ -27,7 +27,7 @@ LIB = PKG / LIB_NAME
 
 CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "prefill_tc.cu", "attention_generic.cu", "kv_append.cu",
               "attention_noalloc.cu",
-              "block_copy.cu", "peer_allreduce.cu"]
+              "block_copy.cu", "peer_allreduce.cu", "oproj_allreduce.cu"]
 CXX_SOURCES = ["step_plan.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -478,6 +478,75 @@ int32_t pa_peer_allreduce(void* const* bases, int32_t world, int32_t rank, int64
   return PA_OK;
 }
 
+int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, int32_t k, const void* w, int32_t n,
+                           int32_t dtype, void* const* bases, int32_t world, int32_t rank, int64_t stage_offset,
+                           int64_t out_offset, int64_t flags_offset, double timeout_s, int32_t* error_word,
+                           void* stream_ptr) {
+  using namespace pa;
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: rank %d of %d (at most %d ranks)", rank, world, kPeerMax);
+  if (dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_UNSUPPORTED, "oproj_allreduce: dtype code %d (bf16 or fp16 only)", dtype);
+  if (rows < 0 || k <= 0 || k % kOprojKStep || n <= 0 || n % (kOprojTile * world))
+    return fail(PA_ERR_UNSUPPORTED, "oproj_allreduce: rows %d, k %d, n %d (k a multiple of %d, n of %d x %d ranks)",
+                rows, k, n, kOprojKStep, kOprojTile, world);
+  if (a_row_stride < k || a_row_stride % 8 || a_row_stride > (int64_t(1) << 32))
+    return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: a row stride %lld for k %d (a multiple of 8, >= k)",
+                (long long)a_row_stride, k);
+  if (!a || !w || !bases || !error_word || reinterpret_cast<uintptr_t>(a) % 16 || reinterpret_cast<uintptr_t>(w) % 16)
+    return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: NULL or unaligned pointer");
+  if (stage_offset < 0 || out_offset < 0 || flags_offset < 0 || stage_offset % 16 || out_offset % 16 ||
+      flags_offset % 16)
+    return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: offsets must be non-negative multiples of 16");
+  if (!(timeout_s > 0.0) || timeout_s > 600.0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: timeout must be in (0, 600] seconds");
+  OprojParams p{};
+  for (int r = 0; r < world; ++r) {
+    p.base[r] = static_cast<uint8_t*>(bases[r]);
+    if (!p.base[r] || reinterpret_cast<uintptr_t>(p.base[r]) % 16)
+      return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: buffer of rank %d is NULL or not 16-byte aligned", r);
+  }
+  if (rows == 0) return PA_OK;
+  auto fn = encode_fn();
+  if (!fn) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  // a as (k, rows) and w as (k, n): one stage is a (64, 128) box of each, 128-byte swizzle
+  // (rows past `rows` read as zeros).
+  auto kmajor = [&](const void* base, int64_t outer, int64_t stride, CUtensorMap* map) -> int32_t {
+    cuuint64_t gdim[2] = {cuuint64_t(k), cuuint64_t(outer)};
+    cuuint64_t gstride[1] = {cuuint64_t(stride) * 2};
+    cuuint32_t box[2] = {cuuint32_t(kOprojKStep), cuuint32_t(kOprojTile)};
+    cuuint32_t estride[2] = {1u, 1u};
+    CUresult r = fn(map, tma_dtype(dtype), 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    return PA_OK;
+  };
+  CUtensorMap ta, tw;
+  int32_t st = kmajor(a, rows, a_row_stride, &ta);
+  if (st != PA_OK) return st;
+  st = kmajor(w, n, k, &tw);
+  if (st != PA_OK) return st;
+  p.stage_offset = stage_offset;
+  p.out_offset = out_offset;
+  p.flags_offset = flags_offset;
+  p.rows = rows;
+  p.k = k;
+  p.n = n;
+  p.world = world;
+  p.rank = rank;
+  p.timeout_ns = uint64_t(timeout_s * 1e9);
+  p.err = error_word;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t vecs = int64_t(rows) * (n / world) * 2 / 16;  // 16-byte vectors of this rank's slice
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(sms, (vecs + kPeerThreads - 1) / kPeerThreads)));
+  cudaError_t e = launch_oproj_allreduce(dtype, ta, tw, p, grid, static_cast<cudaStream_t>(stream_ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "oproj_allreduce launch");
+  return PA_OK;
+}
+
 int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream_ptr) {
   using namespace pa;
   if (!workspace || !error_word) return fail(PA_ERR_INVALID_ARGUMENT, "NULL pointer");

@@ -129,6 +129,24 @@ struct PeerReduceParams {
   int* err;
 };
 
+// The o_proj GEMM fused with its all-reduce (oproj_allreduce.cu).  Each rank's mapped
+// buffer holds a staging area [world][rows][n / world] (16-bit partials pushed by every
+// rank into the owner of those columns), output slots [rows][n] and the flag area above;
+// the gather launch counts its finished CTAs in [kPeerCounter2].
+constexpr int kPeerCounter2 = 18;
+constexpr int kOprojTile = 128;       // output rows and columns of one GEMM CTA
+constexpr int kOprojKStep = 64;       // k per pipeline stage (one 128-byte swizzled row)
+struct OprojParams {
+  uint8_t* base[kPeerMax];
+  int64_t stage_offset;       // byte offset of the staging area
+  int64_t out_offset;         // byte offset of this call's output slot
+  int64_t flags_offset;
+  int32_t rows, k, n;         // a is [rows, k], w is [n, k] (K-major), the output [rows, n]
+  int32_t world, rank;
+  uint64_t timeout_ns;
+  int* err;
+};
+
 // Returns true when the fast decode kernel has an instantiation for this shape.
 bool decode_supported(int dtype, int head_dim, int group, int block_size);
 // Dynamic shared memory bytes of the decode kernel.
@@ -149,5 +167,8 @@ cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensor
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);
+// ta: a as (k, rows), tw: w as (k, n); both boxes (64, 128) with 128-byte swizzle.
+cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const OprojParams& p,
+                                   int gather_grid, cudaStream_t stream);
 
 }  // namespace pa

@@ -1,8 +1,11 @@
-"""The NVLink peer-memory all-reduce (tensor_parallel.PeerAllReduce, the C ABI's
-pa_peer_allreduce) on two GPUs: its sums are bitwise the float32 rank-order sum rounded
-once, identical on every rank, across repeated calls (epochs and slot reuse); the KV-head
-tensor-parallel layer gives the same result through it as through NCCL; and a peer that
-never joins ends the call with a timeout error instead of a hang.  Skipped with fewer than
+"""The NVLink peer-memory collectives on two GPUs.  The all-reduce
+(tensor_parallel.PeerAllReduce, the C ABI's pa_peer_allreduce): its sums are bitwise the
+float32 rank-order sum rounded once, identical on every rank, across repeated calls (epochs
+and slot reuse); the KV-head tensor-parallel layer gives the same result through it as
+through NCCL; and a peer that never joins ends the call with a timeout error instead of a
+hang.  The o_proj GEMM fused with its all-reduce (FusedOProjAllReduce,
+pa_oproj_allreduce): the sum of the ranks' rounded products on both ranks, byte-identical
+across ranks, and the same layer output as NCCL.  Skipped with fewer than
 two GPUs.  NVLS is off (NCCL_NVLS_ENABLE=0) and the collective maps peers with plain CUDA
 IPC, so no rank's memory is bound to a multicast object."""
 
@@ -88,6 +91,42 @@ def _worker(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
             dist.barrier()
             np.save(os.path.join(out_dir, f"peer{rank}.npy"), peer.float().cpu().numpy())
             np.save(os.path.join(out_dir, f"nccl{rank}.npy"), nccl.float().cpu().numpy())
+        elif mode == "fused":
+            for dtype in (torch.bfloat16, torch.float16):
+                fused = tp.FusedOProjAllReduce(512, 1024, dtype, device=dev, timeout_s=5.0)
+                for it, (rows, k) in enumerate([(512, 1024), (200, 256), (512, 1024), (77, 128)]):
+                    a = [torch.randn(rows, k, generator=torch.Generator().manual_seed(1000 * it + r)).to(dtype)
+                         for r in range(world)]
+                    w = [(torch.randn(1024, k, generator=torch.Generator().manual_seed(2000 * it + r)) / k ** 0.5)
+                         .to(dtype) for r in range(world)]
+                    out = fused(a[rank].to(dev), w[rank].to(dev))
+                    torch.cuda.synchronize(dev)
+                    got = out.double().cpu()
+                    # each rank's product rounded to the dtype, summed, rounded once
+                    ref = sum((a[r].double() @ w[r].double().t()).to(dtype).double() for r in range(world))
+                    key = f"{dtype}-{it}"
+                    result[key] = float((got - ref).abs().max() / ref.abs().max())
+                    np.save(os.path.join(out_dir, f"f{rank}-{key}.npy"), got.numpy())
+                fused.check()
+                fused.close()
+                dist.barrier()
+        elif mode == "fused_layer":
+            from test_gpu_tensor_parallel import D, HEADS, KV_HEADS, _inputs, _layer_args
+
+            batch = _inputs()
+            qs, ks = tp.kv_head_shard(HEADS, KV_HEADS, rank, world)
+            w_o = tp.o_proj_shard(batch[8], HEADS, D, rank, world, KV_HEADS).to(dev)
+            args = _layer_args(dev, qs, ks, batch)
+            fused = tp.FusedOProjAllReduce(args[0].shape[0], w_o.shape[1], torch.bfloat16, device=dev, timeout_s=5.0)
+            got = tp.KVHeadParallelAttention(w_o=w_o, fused=fused)(*args).clone()
+            args = _layer_args(dev, qs, ks, batch)
+            nccl = tp.KVHeadParallelAttention(w_o=w_o)(*args)
+            torch.cuda.synchronize(dev)
+            fused.check()
+            fused.close()
+            dist.barrier()
+            np.save(os.path.join(out_dir, f"fused{rank}.npy"), got.float().cpu().numpy())
+            np.save(os.path.join(out_dir, f"nccl{rank}.npy"), nccl.float().cpu().numpy())
         elif mode == "timeout":
             red = tp.PeerAllReduce(4096, torch.float32, timeout_s=0.5)
             if rank == 0:                                  # rank 1 never joins this call
@@ -138,6 +177,28 @@ def test_tensor_parallel_layer_through_peer_allreduce_matches_nccl(tmp_path):
         np.testing.assert_allclose(np.load(tmp_path / f"peer{r}.npy"), np.load(tmp_path / f"nccl{r}.npy"),
                                    atol=2e-2, rtol=2e-2)
     np.testing.assert_array_equal(np.load(tmp_path / "peer0.npy"), np.load(tmp_path / "peer1.npy"))
+
+
+@needs_two
+def test_fused_oproj_allreduce_is_the_sum_of_rounded_products(tmp_path):
+    """The GEMM whose epilogue pushes tiles to their owners, then the owners' sums: within
+    a few units in the last place of the float64 reference, and the same bytes on both ranks."""
+    res = _spawn(tmp_path, "fused")
+    for r in range(2):
+        assert len(res[r]) == 8, res[r]
+        for key, err in res[r].items():
+            assert err < (2e-2 if "bfloat16" in key else 3e-3), (key, err)
+    for f in sorted(tmp_path.glob("f0-*.npy")):
+        np.testing.assert_array_equal(np.load(f), np.load(tmp_path / f.name.replace("f0-", "f1-")))
+
+
+@needs_two
+def test_tensor_parallel_layer_through_fused_oproj_matches_nccl(tmp_path):
+    _spawn(tmp_path, "fused_layer")
+    for r in range(2):
+        np.testing.assert_allclose(np.load(tmp_path / f"fused{r}.npy"), np.load(tmp_path / f"nccl{r}.npy"),
+                                   atol=2e-2, rtol=2e-2)
+    np.testing.assert_array_equal(np.load(tmp_path / "fused0.npy"), np.load(tmp_path / "fused1.npy"))
 
 
 @needs_two

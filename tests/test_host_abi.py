@@ -20,7 +20,7 @@ REFERENCE_SIGNATURE = ["query", "k_pool", "v_pool", "block_tables", "context_len
 def test_library_exports_every_declared_symbol(pkg):
     lib = pkg._lib.lib()
     declared = pkg._lib.declared_symbols()
-    assert len(declared) == 19
+    assert len(declared) == 20
     for name in declared:
         assert hasattr(lib, name), name
     dyn = subprocess.run(["nm", "-D", "--defined-only", str(pkg._lib.LIB_PATH)], capture_output=True,
@@ -243,3 +243,39 @@ def test_multi_gpu_and_block_entry_points_reject_bad_arguments(pkg):
     with pytest.raises(ValueError):
         pkg._lib.check(lib.pa_ipc_open(None, 0, None))
     assert pkg.metadata.prefill_tile_rows() == lib.pa_prefill_tile_rows() > 0
+
+
+def test_fused_oproj_allreduce_rejects_bad_arguments(pkg):
+    """pa_oproj_allreduce checks shapes, dtypes, alignment and ranks on the host before any
+    device work; zero rows is a no-op."""
+    import ctypes
+
+    lib = pkg._lib.lib()
+    err = ctypes.c_int32(0)
+    fake = 1 << 20                      # aligned, never dereferenced by the host checks
+    bases = (ctypes.c_void_p * 2)(fake, fake)
+
+    def call(rows=256, k=1024, n=1024, dtype=2, world=2, rank=0, a=fake, a_stride=1024, w=fake, stage=0, out=4096,
+             flags=8192, timeout=1.0, b=bases):
+        return lib.pa_oproj_allreduce(a, a_stride, rows, k, w, n, dtype, b, world, rank, stage, out, flags, timeout,
+                                      ctypes.addressof(err), None)
+
+    with pytest.raises(ValueError, match="rank 2 of 2"):
+        pkg._lib.check(call(rank=2))
+    with pytest.raises(NotImplementedError, match="bf16 or fp16"):
+        pkg._lib.check(call(dtype=0))
+    with pytest.raises(NotImplementedError, match="k a multiple of 64"):
+        pkg._lib.check(call(k=1000, a_stride=1000))
+    with pytest.raises(NotImplementedError, match="n of 128 x 2 ranks"):
+        pkg._lib.check(call(n=384))
+    with pytest.raises(ValueError, match="row stride"):
+        pkg._lib.check(call(a_stride=1020))
+    with pytest.raises(ValueError, match="unaligned pointer"):
+        pkg._lib.check(call(a=fake + 8))
+    with pytest.raises(ValueError, match="offsets"):
+        pkg._lib.check(call(out=4100))
+    with pytest.raises(ValueError, match="timeout"):
+        pkg._lib.check(call(timeout=0.0))
+    with pytest.raises(ValueError, match="rank 1 is NULL"):
+        pkg._lib.check(call(b=(ctypes.c_void_p * 2)(fake, None)))
+    pkg._lib.check(call(rows=0))        # nothing to do, nothing launched
