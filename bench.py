@@ -454,14 +454,24 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
         marks = [[[ev() for _ in range(4)] for _ in range(L)] for _ in range(args.steps)]
         t0, t1 = ev(), ev()
         t0.record(stream)
+        host_step_ms = []
         for k in range(args.steps):
+            th = time.perf_counter()
             step(metas[args.warmup + k], marks[k])
+            host_step_ms.append((time.perf_counter() - th) * 1e3)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
         elapsed = t0.elapsed_time(t1)
         attn_kernels = pkg._lib.last_launches()      # this library's kernels per attention call
         attn_ms = float(np.mean([m[0].elapsed_time(m[1]) for mk in marks for m in mk]))
+        # rank 0's spread: per-layer attention spans and the host's enqueue time per step
+        # (a span far above the kernels' own time means the GPU waited for the host)
+        spans = [m[0].elapsed_time(m[1]) for mk in marks for m in mk]
+        spread = {"attn_span_ms_min_p50_max": [round(min(spans), 3), round(float(np.median(spans)), 3),
+                                               round(max(spans), 3)],
+                  "attn_span_ms_first_step": [round(x, 3) for x in spans[:L]],
+                  "host_enqueue_ms_per_step": [round(x, 2) for x in host_step_ms]}
         gemm_ms = float(np.mean([m[1].elapsed_time(m[2]) for mk in marks for m in mk]))
         ar_ms = float(np.mean([m[2].elapsed_time(m[3]) for mk in marks for m in mk]))
 
@@ -536,6 +546,7 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
         "e2e": {"value": B * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": words * 4 // args.steps + L * B * (Hq + 2 * Hkv) * D * 2,
                 "d2h_bytes_per_step": B * DM * 2, "ms_per_step": e2e_ms / args.steps},
+        "launch_spread": spread,
         "gpu_launches": args.steps * L * (1 + len(attn_kernels) + (1 if reducer is not None else 0)
                                           + (2 if fused is not None else 0)),
         "clocks": clocks.summary(),

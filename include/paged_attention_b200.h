@@ -303,7 +303,7 @@ int32_t pa_peer_allreduce(void* const* bases, int32_t world, int32_t rank, int64
  *   a             this rank's [rows, k] activations (row stride a_row_stride elements,
  *                 a multiple of 8; 16-byte aligned)
  *   w             this rank's o_proj slice, K-major [n, k] contiguous (16-byte aligned)
- *   k, n          k a multiple of 64; n a multiple of 128 * world
+ *   k, n          k a multiple of 64; n a multiple of 256 * world
  *   bases         HOST array of `world` device pointers: every rank's buffer (CUDA IPC),
  *                 same layout on all ranks: a staging area of rows * n elements at
  *                 stage_offset, the output [rows, n] at out_offset, a zero-initialised

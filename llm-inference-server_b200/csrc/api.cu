@@ -487,9 +487,9 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
     return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: rank %d of %d (at most %d ranks)", rank, world, kPeerMax);
   if (dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
     return fail(PA_ERR_UNSUPPORTED, "oproj_allreduce: dtype code %d (bf16 or fp16 only)", dtype);
-  if (rows < 0 || k <= 0 || k % kOprojKStep || n <= 0 || n % (kOprojTile * world))
+  if (rows < 0 || k <= 0 || k % kOprojKStep || n <= 0 || n % (kOprojTileN * world))
     return fail(PA_ERR_UNSUPPORTED, "oproj_allreduce: rows %d, k %d, n %d (k a multiple of %d, n of %d x %d ranks)",
-                rows, k, n, kOprojKStep, kOprojTile, world);
+                rows, k, n, kOprojKStep, kOprojTileN, world);
   if (a_row_stride < k || a_row_stride % 8 || a_row_stride > (int64_t(1) << 32))
     return fail(PA_ERR_INVALID_ARGUMENT, "oproj_allreduce: a row stride %lld for k %d (a multiple of 8, >= k)",
                 (long long)a_row_stride, k);
@@ -509,12 +509,12 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
   if (rows == 0) return PA_OK;
   auto fn = encode_fn();
   if (!fn) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
-  // a as (k, rows) and w as (k, n): one stage is a (64, 128) box of each, 128-byte swizzle
-  // (rows past `rows` read as zeros).
-  auto kmajor = [&](const void* base, int64_t outer, int64_t stride, CUtensorMap* map) -> int32_t {
+  // a as (k, rows) and w as (k, n): one stage is a (64, 128) box of a and a (64, 256) box
+  // of w, 128-byte swizzle (rows past `rows` read as zeros).
+  auto kmajor = [&](const void* base, int64_t outer, int64_t stride, int box_rows, CUtensorMap* map) -> int32_t {
     cuuint64_t gdim[2] = {cuuint64_t(k), cuuint64_t(outer)};
     cuuint64_t gstride[1] = {cuuint64_t(stride) * 2};
-    cuuint32_t box[2] = {cuuint32_t(kOprojKStep), cuuint32_t(kOprojTile)};
+    cuuint32_t box[2] = {cuuint32_t(kOprojKStep), cuuint32_t(box_rows)};
     cuuint32_t estride[2] = {1u, 1u};
     CUresult r = fn(map, tma_dtype(dtype), 2, const_cast<void*>(base), gdim, gstride, box, estride,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -523,9 +523,9 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
     return PA_OK;
   };
   CUtensorMap ta, tw;
-  int32_t st = kmajor(a, rows, a_row_stride, &ta);
+  int32_t st = kmajor(a, rows, a_row_stride, kOprojTile, &ta);
   if (st != PA_OK) return st;
-  st = kmajor(w, n, k, &tw);
+  st = kmajor(w, n, k, kOprojTileN, &tw);
   if (st != PA_OK) return st;
   p.stage_offset = stage_offset;
   p.out_offset = out_offset;

@@ -134,7 +134,8 @@ struct PeerReduceParams {
 // rank into the owner of those columns), output slots [rows][n] and the flag area above;
 // the gather launch counts its finished CTAs in [kPeerCounter2].
 constexpr int kPeerCounter2 = 18;
-constexpr int kOprojTile = 128;       // output rows and columns of one GEMM CTA
+constexpr int kOprojTile = 128;       // output rows of one GEMM CTA
+constexpr int kOprojTileN = 256;      // output columns of one GEMM CTA
 constexpr int kOprojKStep = 64;       // k per pipeline stage (one 128-byte swizzled row)
 struct OprojParams {
   uint8_t* base[kPeerMax];
@@ -167,7 +168,7 @@ cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensor
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);
-// ta: a as (k, rows), tw: w as (k, n); both boxes (64, 128) with 128-byte swizzle.
+// ta: a as (k, rows), box (64, 128); tw: w as (k, n), box (64, 256); 128-byte swizzle.
 cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const OprojParams& p,
                                    int gather_grid, cudaStream_t stream);
 

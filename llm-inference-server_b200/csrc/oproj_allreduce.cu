@@ -6,12 +6,14 @@
 // `world` contiguous slices of n / world; rank s owns slice s.  Two launches per call,
 // and every access to another GPU's memory is a plain 16-byte store:
 //
-//   oproj_push_kernel   one CTA per 128 x 128 output tile.  Warp 4 streams 64-wide k
-//     steps of a and w with TMA (128-byte swizzle) into a 3-stage ring, warp 5 issues
-//     tcgen05 MMAs (M = N = 128, both operands K-major) into a 128-column TMEM
-//     accumulator, and warps 0-3 round the finished tile to the storage dtype, stage it in
-//     the freed ring and store it, 256-byte row pieces at a time, into the staging area
-//     of the rank owning those columns: the reduce-scatter is the GEMM's epilogue.  The
+//   oproj_push_kernel   one CTA per 128 x 256 output tile (one CTA per SM).  Warp 4
+//     streams 64-wide k steps of a and w with TMA (128-byte swizzle) into a 4-stage ring,
+//     warp 5 issues tcgen05 MMAs (M = 128, N = 256, both operands K-major) into a
+//     256-column TMEM accumulator, and warps 0-3 round the finished tile to the storage
+//     dtype, stage it in the freed ring and store it, 512-byte row pieces at a time, into
+//     the staging area of the rank owning those columns: the reduce-scatter is the GEMM's
+//     epilogue.  The wide tile matters because the GEMM is fed from L2 at a fixed rate
+//     per SM: 128 x 256 moves a quarter fewer bytes per flop than 128 x 128.  The
 //     last CTA to finish releases this rank's "ready" flag into every rank's flag area.
 //   oproj_gather_kernel the owner waits for every rank's ready flag, sums its slice over
 //     the `world` staged partials in rank order in float32 (so every rank receives the
@@ -31,14 +33,16 @@
 
 namespace pa {
 
-constexpr int kOpStages = 3;
+constexpr int kOpStages = 4;
 constexpr int kOpThreads = 192;
-constexpr int kOpBox = kOprojTile * 128;        // one 128-row x 64-element box (16-bit)
-constexpr int kOpStage = 2 * kOpBox;            // a box, then w box
-constexpr int kOpPitch = kOprojTile * 2 + 16;   // staged output row: 256 bytes + 16 (bank spread)
+constexpr int kOpBoxA = kOprojTile * 128;       // 128 rows x 64 elements (16-bit)
+constexpr int kOpBoxW = kOprojTileN * 128;      // 256 rows x 64 elements
+constexpr int kOpStage = kOpBoxA + kOpBoxW;     // a box, then w box
+constexpr int kOpPitch = kOprojTileN * 2 + 16;  // staged output row: 512 bytes + 16 (bank spread)
 constexpr int kOpBarOff = kOpStages * kOpStage;
 constexpr int kOpSmem = kOpBarOff + 128;
 static_assert(kOprojTile * kOpPitch <= kOpBarOff, "the output tile reuses the ring");
+static_assert(kOpSmem <= 227 * 1024, "shared memory per CTA");
 
 struct OpBars {
   uint64_t full[kOpStages], empty[kOpStages];
@@ -64,17 +68,17 @@ __device__ __forceinline__ uint32_t pack_pair<__half>(uint32_t lo, uint32_t hi) 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kOpThreads, 2)
+__global__ void __launch_bounds__(kOpThreads, 1)
     oproj_push_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                       const __grid_constant__ OprojParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   OpBars* bars = reinterpret_cast<OpBars*>(smem + kOpBarOff);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kOprojTile, m0 = blockIdx.y * kOprojTile;
+  const int n0 = blockIdx.x * kOprojTileN, m0 = blockIdx.y * kOprojTile;
   const int ksteps = p.k / kOprojKStep;
 
   if (warp == 5) {
-    tmem_alloc(&bars->tmem_base, kOprojTile);
+    tmem_alloc(&bars->tmem_base, kOprojTileN);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -105,14 +109,14 @@ __global__ void __launch_bounds__(kOpThreads, 2)
         uint8_t* st = smem + s * kOpStage;
         mbar_arrive_expect_tx(&bars->full[s], kOpStage);
         tma_load_2d(st, &ta, j * kOprojKStep, m0, &bars->full[s]);
-        tma_load_2d(st + kOpBox, &tw, j * kOprojKStep, n0, &bars->full[s]);
+        tma_load_2d(st + kOpBoxA, &tw, j * kOprojKStep, n0, &bars->full[s]);
       }
       if (!ok) set_error(p.err, kErrWaitTimeout);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16<T>(kOprojTile, kOprojTile, false);
+      constexpr uint32_t idesc = idesc_f16<T>(kOprojTile, kOprojTileN, false);
       bool ok = true;
       for (int j = 0; j < ksteps; ++j) {
         const int s = j % kOpStages;
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kOpThreads, 2)
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + s * kOpStage), w0 = a0 + kOpBox;
+        const uint32_t a0 = smem_u32(smem + s * kOpStage), w0 = a0 + kOpBoxA;
 #pragma unroll
         for (int kk = 0; kk < kOprojKStep / 16; ++kk)
           umma_f16(tacc, smem_desc_sw128(a0 + kk * 32, 16, 1024), smem_desc_sw128(w0 + kk * 32, 16, 1024), idesc,
@@ -141,7 +145,7 @@ __global__ void __launch_bounds__(kOpThreads, 2)
       const int r = warp * 32 + lane;
       const uint32_t lane_base = uint32_t(warp * 32) << 16;
 #pragma unroll
-      for (int c = 0; c < kOprojTile / 32; ++c) {
+      for (int c = 0; c < kOprojTileN / 32; ++c) {
         uint32_t v[32];
         tmem_ld32(tacc + lane_base + 32 * c, v);
         tmem_wait_ld();
@@ -156,13 +160,13 @@ __global__ void __launch_bounds__(kOpThreads, 2)
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
     if (got) {
-      // 16 threads per 256-byte row piece; destination: staging[rank][row][col0 ..] of
-      // the owner of columns n0 .. n0 + 127.
+      // One warp per 512-byte row piece; destination: staging[rank][row][col0 ..] of the
+      // owner of columns n0 .. n0 + 255.
       const int slice = p.n / p.world, owner = n0 / slice, col0 = n0 - owner * slice;
       uint8_t* dst = p.base[owner] + p.stage_offset + (int64_t(p.rank) * p.rows * slice + col0) * 2;
-      const int ch = tid & 15;
+      const int ch = tid & 31;
 #pragma unroll 4
-      for (int row = tid >> 4; row < kOprojTile; row += 8) {
+      for (int row = tid >> 5; row < kOprojTile; row += 4) {
         if (m0 + row < p.rows) {
           const uint4 v = *reinterpret_cast<const uint4*>(smem + row * kOpPitch + ch * 16);
           *reinterpret_cast<uint4*>(dst + int64_t(m0 + row) * slice * 2 + ch * 16) = v;
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(kOpThreads, 2)
   }
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tacc, kOprojTile);
+    tmem_dealloc(tacc, kOprojTileN);
   }
 }
 
@@ -280,7 +284,7 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const 
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(p.n / kOprojTile, (p.rows + kOprojTile - 1) / kOprojTile);
+  dim3 grid(p.n / kOprojTileN, (p.rows + kOprojTile - 1) / kOprojTile);
   push<<<grid, kOpThreads, kOpSmem, stream>>>(ta, tw, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -43,7 +43,7 @@ def _assert_one_ulp(got: torch.Tensor, ref: torch.Tensor, dtype) -> None:
 @pytest.mark.parametrize("rows,k,n,dtype,a_stride", [
     (512, 1024, 1024, torch.bfloat16, None),     # the config-5 tp8 shape, narrowed to n = 1024
     (200, 256, 512, torch.bfloat16, 320),        # partial last row tile, strided activations
-    (1, 64, 128, torch.float16, None),           # one row, one k step, fp16
+    (1, 64, 256, torch.float16, None),           # one row, one k step, fp16
 ])
 def test_single_rank_is_the_rounded_product(pkg, rows, k, n, dtype, a_stride):
     fused = _tp(pkg).FusedOProjAllReduce(512, n, dtype, device=DEV)
@@ -80,8 +80,8 @@ def test_tensor_parallel_layer_uses_the_fused_gemm(pkg):
     args = _layer_args(DEV, qs, ks, batch)
     rows = args[0].shape[0]
     n = w_o.shape[1]
-    if n % 128:
-        pytest.skip(f"d_model {n} is not a multiple of the fused GEMM's 128-column tile")
+    if n % 256:
+        pytest.skip(f"d_model {n} is not a multiple of the fused GEMM's 256-column tile")
     fused = tp.FusedOProjAllReduce(rows, n, torch.bfloat16, device=DEV)
     got = tp.KVHeadParallelAttention(w_o=w_o, fused=fused)(*args).clone()
     args = _layer_args(DEV, qs, ks, batch)

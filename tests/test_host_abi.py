@@ -266,7 +266,7 @@ def test_fused_oproj_allreduce_rejects_bad_arguments(pkg):
         pkg._lib.check(call(dtype=0))
     with pytest.raises(NotImplementedError, match="k a multiple of 64"):
         pkg._lib.check(call(k=1000, a_stride=1000))
-    with pytest.raises(NotImplementedError, match="n of 128 x 2 ranks"):
+    with pytest.raises(NotImplementedError, match="n of 256 x 2 ranks"):
         pkg._lib.check(call(n=384))
     with pytest.raises(ValueError, match="row stride"):
         pkg._lib.check(call(a_stride=1020))
