@@ -337,6 +337,9 @@ WORKLOADS = {
     "config4": dict(heads=32, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=0.0, median_ctx=None,
                     lo=0, hi=0, layers=32, churn=0.0, batch=64),
     # Whole-block moves on the config-3 pool shape: copy-on-write and swap-out / swap-in.
+    # config 5's per-rank o_proj alone (rows = batch, k = heads * head_dim / --tp, n = d_model).
+    "oproj": dict(heads=64, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=0.0, median_ctx=None,
+                  lo=0, hi=0, layers=1, churn=0.0, batch=512, d_model=8192),
     "blocks": dict(heads=32, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=0.0, median_ctx=None,
                    lo=0, hi=0, layers=32, churn=0.0),
 }
@@ -1010,6 +1013,75 @@ def _blocks_cpu_sample(args) -> dict:
                       "copy of the input pools"}
 
 
+def run_oproj(args, rank: int, world: int, local_rank: int) -> None:
+    """``--workload oproj``: config 5's per-rank output projection on one GPU -- rows =
+    ``--batch`` (512), k = 64 heads x 128 / ``--tp``, n = d_model 8192, bf16 -- through the
+    fused collective's kernels with one rank (the tcgen05 GEMM whose epilogue stages the
+    tiles, then the owner pass that writes the output) and through cuBLAS (torch.matmul).
+    Each step runs one call per weight copy, cycling over enough copies (>= 256 MB) that a
+    call's weights are not left in the 126 MB L2 by the previous one.  CUDA events on the
+    launching stream; one JSON line."""
+    import importlib
+
+    from __graft_entry__ import import_package
+
+    pkg = import_package()
+    tpm = importlib.import_module(f"{pkg.__name__}.tensor_parallel")
+    w = WORKLOADS["oproj"]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    rows, n = args.batch, w["d_model"]
+    k = w["heads"] * w["head_dim"] // args.tp
+    copies = max(2, -(-256 * 2 ** 20 // (n * k * 2)))
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    a = torch.randn(rows, k, generator=g, device=dev).to(torch.bfloat16)
+    w_nk = [(torch.randn(n, k, generator=g, device=dev) / k ** 0.5).to(torch.bfloat16) for _ in range(copies)]
+    w_kn = [t.t().contiguous() for t in w_nk]
+    fused = tpm.FusedOProjAllReduce(rows, n, torch.bfloat16, device=dev)
+    out = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            for c in range(copies):
+                fn(c)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for c in range(copies):
+                fn(c)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / (args.steps * copies)
+
+    clocks = ClockSampler(dev.index)
+    with clocks, QuietHost():
+        fused_ms = timed(lambda c: fused(a, w_nk[c]))
+        cublas_ms = timed(lambda c: torch.matmul(a, w_kn[c], out=out))
+    fused.check()
+    flops = 2.0 * rows * k * n
+    _, bf16_peak, peak_kind = _measured_peaks()
+    line = {
+        "metric": "config-5 o_proj per call: fused tcgen05 GEMM (+ owner pass) vs cuBLAS", "unit": "TFLOP/s",
+        "value": flops / (fused_ms / 1e3) / 1e12, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": fused_ms * copies, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"o_proj of one rank at tp{args.tp}: [{rows}, {k}] x [{k}, {n}] bf16",
+                   "weight_copies": copies, "l2": f"{copies} weight copies of {n * k * 2 / 2 ** 20:.0f} MB cycled"},
+        "fused_us": fused_ms * 1e3, "cublas_us": cublas_ms * 1e3,
+        "cublas_tflops": flops / (cublas_ms / 1e3) / 1e12,
+        "roofline": {"bound": "tensor", "achieved": flops / (fused_ms / 1e3) / 1e12, "peak": bf16_peak,
+                     "unit": "TFLOP/s", "frac": flops / (fused_ms / 1e3) / 1e12 / bf16_peak,
+                     "peak_source": f"{peak_kind} sustained bf16", "traffic": None,
+                     "kernel": "oproj_push_kernel + oproj_gather_kernel (one rank)"},
+        "cpu_baseline": None, "e2e": None,
+        "gpu_launches": 2 * (args.warmup + args.steps) * copies,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_blocks(args, rank: int, world: int, local_rank: int) -> None:
     """``--workload blocks``: one step = copy-on-write of BLOCK_COW_PAIRS blocks in every
     layer (one launch), then swap-out of BLOCK_SWAP blocks to pinned host memory and
@@ -1443,6 +1515,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graphs", action="store_true",
                     help="config4: run the decode pass as a captured CUDA graph per step")
+    ap.add_argument("--tp", type=int, default=2, help="oproj: the tensor-parallel size whose per-rank k is run")
     ap.add_argument("--allreduce", choices=["peer", "nccl", "fused"], default="peer",
                     help="config5: the o_proj all-reduce over NVLink peer memory (default), NCCL, or fused "
                          "with the o_proj GEMM into one peer-memory collective")
@@ -1471,7 +1544,11 @@ def main() -> None:
             torch.distributed.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     try:
         if args.impl == "reference":
-            if args.workload == "blocks":
+            if args.workload == "oproj":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable": "the reference has no tensor-parallel "
+                                      "o_proj (no multi-GPU path); --workload oproj is a GEMM microbenchmark"}))
+            elif args.workload == "blocks":
                 if rank == 0:
                     cpu = _blocks_cpu_sample(args)
                     print(json.dumps({"impl": "reference", "metric": "KV block moves: copy-on-write GB/s (device) "
@@ -1485,6 +1562,8 @@ def main() -> None:
             run_blocks(args, rank, world, local_rank)
         elif args.workload == "config5":
             run_tp(args, rank, world, local_rank)
+        elif args.workload == "oproj":
+            run_oproj(args, rank, world, local_rank)
         elif args.workload == "config4":
             run_prefix(args, rank, world, local_rank)
         elif args.workload == "config1":
