@@ -12,9 +12,9 @@
 //     256-column TMEM accumulator, and warps 0-3 round the finished tile to the storage
 //     dtype, stage it in the freed ring and store it, 512-byte row pieces at a time, into
 //     the staging area of the rank owning those columns: the reduce-scatter is the GEMM's
-//     epilogue.  The wide tile matters because the GEMM is fed from L2 at a fixed rate
-//     per SM: 128 x 256 moves a quarter fewer bytes per flop than 128 x 128.  The
-//     last CTA to finish releases this rank's "ready" flag into every rank's flag area.
+//     epilogue.  128 x 256 moves a quarter fewer bytes per flop than 128 x 128 tiles,
+//     which were measured slower in this kernel.  The last CTA to finish releases this
+//     rank's "ready" flag into every rank's flag area.
 //   oproj_gather_kernel the owner waits for every rank's ready flag, sums its slice over
 //     the `world` staged partials in rank order in float32 (so every rank receives the
 //     same bytes), rounds once and stores the sum into every rank's output slot: the

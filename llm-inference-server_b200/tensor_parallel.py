@@ -153,7 +153,7 @@ class FusedOProjAllReduce:
     """The row-split o_proj GEMM and its all-reduce as one collective over NVLink peer
     memory (the C ABI's ``pa_oproj_allreduce``): every rank gets ``sum_r a_r @ w_r``.
 
-    The GEMM (tcgen05, 128 x 128 output tiles) stores each finished tile straight into the
+    The GEMM (tcgen05, 128 x 256 output tiles) stores each finished tile straight into the
     staging area of the rank that owns those columns, so the reduce-scatter rides on the
     GEMM's epilogue; each owner then sums its columns over the ranks' partials in rank
     order (float32) and stores them into every rank's output.  Every access to another
