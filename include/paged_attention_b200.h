@@ -77,10 +77,13 @@ typedef struct pa_step_plan {
   int64_t words;               /* int32 words used in the packed buffer */
 } pa_step_plan;
 
-/* Version of this ABI (bumped on any signature or struct change). */
+/* Version of this ABI (bumped on any signature or struct change).  No reference
+ * counterpart (the reference is one Python package). */
 int32_t pa_abi_version(void);
 
-/* Message of the calling thread's last failed call ("" if none). */
+/* Message of the calling thread's last failed call ("" if none).  No reference
+ * counterpart: the reference raises; the Python binding turns this message into the
+ * reference's exception (ValueError / NotImplementedError) with the same text. */
 const char* pa_last_error(void);
 
 /* Kernels launched by the calling thread's most recent pa_paged_attention_fwd or
@@ -96,6 +99,7 @@ int32_t pa_last_launches(void);
 /*
  * Upper bound on the int32 words pa_plan_step writes for a step with num_seqs
  * sequences, num_tokens packed tokens and at most max_blocks_per_seq blocks per row.
+ * No reference counterpart (sizes the packed buffer that replaces _pack's six tensors).
  */
 int64_t pa_plan_words_bound(int32_t num_seqs, int32_t num_tokens, int32_t max_blocks_per_seq);
 
@@ -146,10 +150,11 @@ int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, con
 
 /* (token, query-head) rows of one tensor-core prefill tile: plan prefill steps with
  * prefill_tile_tokens = pa_prefill_tile_rows() / (num_heads / num_kv_heads) so their
- * rows take the tcgen05 kernel. */
+ * rows take the tcgen05 kernel.  No reference counterpart. */
 int32_t pa_prefill_tile_rows(void);
 
-/* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape. */
+/* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape.
+ * No reference counterpart (the reference's gather path allocates per call). */
 uint64_t pa_workspace_bytes(const pa_step_plan* plan, int32_t num_heads, int32_t head_dim);
 
 /*
@@ -326,6 +331,7 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
  * set by kernels that met an out-of-range block id or slot (the host checks make this
  * unreachable for planned steps) or a pipeline wait that ran out of its iteration
  * limit.  Synchronises `stream`.  Returns PA_OK and stores the word in *error_word.
+ * No reference counterpart (the reference's torch ops raise on the host).
  */
 int32_t pa_read_device_error(void* workspace, int32_t clear, int32_t* error_word, void* stream);
 

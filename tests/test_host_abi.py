@@ -29,6 +29,22 @@ def test_library_exports_every_declared_symbol(pkg):
         assert f" T {name}" in dyn, f"{name} is not a dynamic export"
 
 
+def test_every_entry_point_cites_its_reference_interface_or_has_none(pkg):
+    """Each declaration's doc block (the nearest comment opening at column 0 before it)
+    names the reference interface it replaces (inference_server/...:line) or says it has
+    no counterpart in the reference."""
+    import re
+
+    text = pkg._lib.HEADER.read_text()
+    blocks = [(m.start(), re.sub(r"\s*\n\s*\*?\s?", " ", m.group(0)))
+              for m in re.finditer(r"^/\*.*?\*/", text, flags=re.S | re.M)]
+    for name in pkg._lib.declared_symbols():
+        decl = re.search(rf"^[\w ]+\**\s*\b{name}\(", text, flags=re.M)
+        assert decl, name
+        doc = [b for start, b in blocks if start < decl.start()][-1]
+        assert re.search(r"inference_server/\S+:\s*\d+|counterpart", doc), (name, doc[:200])
+
+
 def test_abi_version_and_struct_size(pkg):
     lib = pkg._lib.lib()
     assert lib.pa_abi_version() == pkg._lib.ABI_VERSION
