@@ -48,8 +48,11 @@ DTYPES = ("f32", "f16", "bf16")
 def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
     """Round float32 values to the storage dtype, returned as float32.
 
-    bf16 uses round-to-nearest-even on the float32 bit pattern (the IEEE rule torch
-    applies when it narrows float32 to bfloat16); f16 goes through numpy's half type.
+    The reference narrows at two points: the probabilities, ``softmax(..., dtype=float32)
+    .to(v.dtype)`` (inference_server/core/attention.py:152 and :184), and every tensor op
+    whose inputs are half precision (its matmuls return the input dtype).  bf16 uses
+    round-to-nearest-even on the float32 bit pattern (the IEEE rule torch applies when it
+    narrows float32 to bfloat16); f16 goes through numpy's half type.
     """
     x = np.asarray(x, dtype=np.float32)
     if dtype == "f32":
@@ -66,11 +69,13 @@ def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
 
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:
-    """The upper 16 bits of float32 values that are exact bf16 numbers."""
+    """The upper 16 bits of float32 values that are exact bf16 numbers (the storage form
+    of the reference's bfloat16 tensors, compared bit for bit in the golden fixtures)."""
     return (np.asarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
 
 
 def bf16_from_bits(bits: np.ndarray) -> np.ndarray:
+    """float32 values of stored bf16 bit patterns (the inverse of :func:`bf16_bits`)."""
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
@@ -108,6 +113,9 @@ def expand_kv_heads(kv: np.ndarray, num_heads: int) -> np.ndarray:
 
 
 def _softmax_f32(scores: np.ndarray) -> np.ndarray:
+    """Row softmax in float32, the reference's ``torch.softmax(scores, dim=-1,
+    dtype=torch.float32)`` (inference_server/core/attention.py:152, :184); rows masked to
+    -inf contribute exact zeros."""
     m = scores.max(axis=-1, keepdims=True)
     e = np.exp(scores - m, dtype=np.float32)
     return (e / e.sum(axis=-1, keepdims=True, dtype=np.float32)).astype(np.float32)
