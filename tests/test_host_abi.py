@@ -211,6 +211,27 @@ def test_cuda_path_fails_loudly_off_gpu(pkg, monkeypatch):
         pkg.reshape_and_cache(q[:, :3], q[:, :3], pool, pool, torch.zeros(5, dtype=torch.int32))
 
 
+def test_executor_graphs_and_fused_oproj_refuse_what_they_cannot_run(pkg):
+    """The executor and the decode-step graphs need CUDA pools, the fused o_proj
+    collective a 16-bit dtype; each says so before touching a device (no fallback)."""
+    import importlib
+
+    executor = importlib.import_module(f"{pkg.__name__}.executor")
+    graphs = importlib.import_module(f"{pkg.__name__}.graphs")
+    tp = importlib.import_module(f"{pkg.__name__}.tensor_parallel")
+    pool = pkg.KVPool(2, 4, 16, 2, 8, torch.float32, "cpu")
+
+    class Model:
+        config = type("Config", (), {"num_attention_heads": 4})()
+
+    with pytest.raises(NotImplementedError, match="CUDA device"):
+        executor.CudaPagedExecutor(Model(), None, pool)
+    with pytest.raises(NotImplementedError, match="CUDA pools"):
+        graphs.DecodeStepGraph(pool.k, pool.v, 4, 0.5, 2, 4)
+    with pytest.raises(NotImplementedError, match="bf16 or fp16"):
+        tp.FusedOProjAllReduce(8, 256, torch.float32)
+
+
 def test_shape_errors_match_reference(pkg):
     pool = torch.randn(8, 4, 3, 8)
     with pytest.raises(ValueError, match="query must be"):
