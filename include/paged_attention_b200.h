@@ -196,10 +196,13 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
  *
  * The split-K scratch lives in a static device array of PA_NOALLOC_SCRATCH_BYTES that
  * every GPU loading this library reserves until the process exits; steps whose
- * pa_workspace_bytes exceeds it are rejected with PA_ERR_BUFFER_TOO_SMALL.  The first
- * call on a device looks the array's address up (make it before any stream capture).
- * All calls share the array: the kernels' error word in it is cleared at the start of
- * each call, and calls whose GPU work overlaps race on it.  Allocates nothing.
+ * pa_workspace_bytes exceeds it are rejected with PA_ERR_BUFFER_TOO_SMALL (after the same
+ * argument checks as pa_paged_attention_fwd, before anything is enqueued).  The first
+ * call in each CUDA context looks the array's address up and zeroes its error word on
+ * `stream` (make it before any stream capture).  All calls share the array, and calls
+ * whose GPU work overlaps race on it.  The kernels' error word in it is sticky, as a
+ * workspace's is: read and clear it with pa_noalloc_read_device_error.  Allocates
+ * nothing.
  */
 int32_t pa_paged_attention_fwd_noalloc(const void* query, int64_t q_stride_token, int64_t q_stride_head,
                                        int64_t q_stride_dim, int32_t num_tokens, int32_t num_heads,
@@ -208,6 +211,16 @@ int32_t pa_paged_attention_fwd_noalloc(const void* query, int64_t q_stride_token
                                        int32_t dtype, float scale, const pa_step_plan* plan,
                                        const int32_t* meta, void* out, int64_t out_stride_token,
                                        int64_t out_stride_head, void* stream);
+
+/*
+ * Read (and clear, when clear != 0) the device error word inside the static scratch of
+ * pa_paged_attention_fwd_noalloc, for callers that never see a workspace pointer: the
+ * same bits pa_read_device_error reports for a workspace (an out-of-range block id
+ * reached a kernel, a pipeline wait ran out of its limit), accumulated over every
+ * no-allocation call in the current context since the last clear.  Synchronises
+ * `stream`.  Allocates nothing.  No counterpart in the reference.
+ */
+int32_t pa_noalloc_read_device_error(int32_t clear, int32_t* error_word, void* stream);
 
 /*
  * Fused K+V append: write the new tokens' keys and values into both pools at their

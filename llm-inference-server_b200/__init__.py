@@ -20,7 +20,7 @@ from __future__ import annotations
 
 from .attention import paged_attention, paged_attention_cuda, read_device_error
 from .kv_cache import HostBlocks, KVPool, allocate_pool, copy_blocks, reshape_and_cache
-from .metadata import StepMetadata, attach, attached
+from .metadata import StepMetadata, attach, attached, prefill_tile_tokens
 
 __all__ = [
     "paged_attention",
@@ -34,4 +34,5 @@ __all__ = [
     "StepMetadata",
     "attach",
     "attached",
+    "prefill_tile_tokens",
 ]

@@ -35,7 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 class StepPlan(ctypes.Structure):
@@ -95,6 +95,7 @@ _SIGNATURES = {
                                                  c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_float,
                                                  POINTER(StepPlan), c_void_p, c_void_p, c_int64, c_int64,
                                                  c_void_p]),
+    "pa_noalloc_read_device_error": (c_int32, [c_int32, POINTER(c_int32), c_void_p]),
     "pa_copy_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p, c_int32,
                                  c_void_p, c_void_p]),
     "pa_gather_blocks": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int64, c_int64, c_void_p,

@@ -118,6 +118,26 @@ static int32_t cuda_fail(cudaError_t e, const char* what) {
   return fail(PA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+void reset_last_launches() { g_last_launches = 0; }
+
+int32_t check_attention_args(int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t block_size,
+                             int32_t num_kv_heads, int32_t dtype, const pa_step_plan* plan) {
+  if (!plan) return fail(PA_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_UNSUPPORTED, "dtype code %d is not float32, float16 or bfloat16", dtype);
+  if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "heads and head_dim must be positive");
+  if (num_heads % num_kv_heads)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%d query heads not divisible by %d kv heads", num_heads, num_kv_heads);
+  if (head_dim > 256) return fail(PA_ERR_UNSUPPORTED, "head_dim %d > 256 is not supported", head_dim);
+  if (plan->num_tokens != num_tokens)
+    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for %d tokens, query has %d", plan->num_tokens, num_tokens);
+  if (plan->block_size != block_size)
+    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for block_size %d, pool has %d", plan->block_size,
+                block_size);
+  return PA_OK;
+}
+
 }  // namespace pa
 
 extern "C" {
@@ -142,19 +162,8 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
                                void* stream_ptr) {
   using namespace pa;
   g_last_launches = 0;
-  if (!plan) return fail(PA_ERR_INVALID_ARGUMENT, "plan must not be NULL");
-  if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16)
-    return fail(PA_ERR_UNSUPPORTED, "dtype code %d is not float32, float16 or bfloat16", dtype);
-  if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
-    return fail(PA_ERR_INVALID_ARGUMENT, "heads and head_dim must be positive");
-  if (num_heads % num_kv_heads)
-    return fail(PA_ERR_INVALID_ARGUMENT, "%d query heads not divisible by %d kv heads", num_heads, num_kv_heads);
-  if (head_dim > 256) return fail(PA_ERR_UNSUPPORTED, "head_dim %d > 256 is not supported", head_dim);
-  if (plan->num_tokens != num_tokens)
-    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for %d tokens, query has %d", plan->num_tokens, num_tokens);
-  if (plan->block_size != block_size)
-    return fail(PA_ERR_INVALID_ARGUMENT, "plan was built for block_size %d, pool has %d", plan->block_size,
-                block_size);
+  const int32_t bad = check_attention_args(num_tokens, num_heads, head_dim, block_size, num_kv_heads, dtype, plan);
+  if (bad != PA_OK) return bad;
   if (num_tokens == 0) return PA_OK;
   if (!query || !k_pool || !v_pool || !out || !meta || !workspace)
     return fail(PA_ERR_INVALID_ARGUMENT, "NULL device pointer");

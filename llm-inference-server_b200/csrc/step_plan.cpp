@@ -54,7 +54,7 @@ static int choose_split(const std::vector<int>& decode_nblk, int num_kv_heads, i
 
 extern "C" {
 
-int32_t pa_abi_version(void) { return 6; }
+int32_t pa_abi_version(void) { return 7; }
 
 const char* pa_last_error(void) { return pa::last_error(); }
 
