@@ -385,7 +385,7 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
            for _ in range(L)]
     bt = torch.from_numpy(wl.tables).to(dev)
     sm = pkg.metadata.sm_count(dev)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
+    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
     dummy = torch.zeros(1, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -630,7 +630,7 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
     pre = _Pass(L, t_pre, Hq, Hkv, D, torch.bfloat16, dev, g)
     bt = torch.from_numpy(wl.tables).to(dev)
     sm = pkg.metadata.sm_count(dev)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
+    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
     dummy = torch.zeros(1, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -1229,7 +1229,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     L, B, Hq, Hkv, D, BS = wl.layers, wl.batch, wl.heads, wl.kv_heads, wl.head_dim, wl.block_size
     f32 = WORKLOADS[args.workload]["dtype"] == "f32"
     dtype, elem = (torch.float32, 4) if f32 else (torch.bfloat16, 2)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv)
+    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
     sm = pkg.metadata.sm_count(dev)
 
     # ---- device-resident inputs

@@ -94,6 +94,7 @@ const char* pa_last_error(void);
 #define PA_LAUNCH_COMBINE 4         /* split-K combine */
 #define PA_LAUNCH_PREFILL_TC 8      /* tcgen05 varlen prefill */
 #define PA_LAUNCH_GENERIC 16        /* generic ragged kernel */
+#define PA_LAUNCH_PREFILL_PAIR 32   /* tcgen05 varlen prefill on CTA pairs (head_dim 128) */
 int32_t pa_last_launches(void);
 
 /*
@@ -148,10 +149,13 @@ int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, con
                               int32_t items_cap, int32_t combine_cap, int32_t* meta_out, int64_t meta_capacity,
                               pa_step_plan* plan);
 
-/* (token, query-head) rows of one tensor-core prefill tile: plan prefill steps with
- * prefill_tile_tokens = pa_prefill_tile_rows() / (num_heads / num_kv_heads) so their
- * rows take the tcgen05 kernel.  No reference counterpart. */
-int32_t pa_prefill_tile_rows(void);
+/* (token, query-head) rows of one tensor-core prefill tile at this head_dim (128: the
+ * single-CTA tcgen05 kernel): plan prefill steps with prefill_tile_tokens =
+ * pa_prefill_tile_rows(head_dim) / (num_heads / num_kv_heads) so their rows take it.  At
+ * head_dim 128 a plan tiled at 256 rows runs on the CTA-pair tcgen05 kernel instead (half
+ * the K/V bytes per SM; measured slower on B200, so not the default).  No reference
+ * counterpart. */
+int32_t pa_prefill_tile_rows(int32_t head_dim);
 
 /* Device workspace bytes pa_paged_attention_fwd needs for this plan and head shape.
  * No reference counterpart (the reference's gather path allocates per call). */

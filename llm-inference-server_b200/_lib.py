@@ -34,6 +34,7 @@ PA_LAUNCH_DECODE_SIMT = 2
 PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
+PA_LAUNCH_PREFILL_PAIR = 32
 
 ABI_VERSION = 7
 
@@ -76,7 +77,7 @@ class StepPlan(ctypes.Structure):
 
 _SIGNATURES = {
     "pa_abi_version": (c_int32, []),
-    "pa_prefill_tile_rows": (c_int32, []),
+    "pa_prefill_tile_rows": (c_int32, [c_int32]),
     "pa_last_launches": (c_int32, []),
     "pa_last_error": (c_char_p, []),
     "pa_plan_words_bound": (c_int64, [c_int32, c_int32, c_int32]),
@@ -148,7 +149,8 @@ def last_launches() -> set[str]:
     """Names of the kernels the calling thread's last attention call launched."""
     mask = lib().pa_last_launches()
     names = {PA_LAUNCH_DECODE_MMA: "decode_mma", PA_LAUNCH_DECODE_SIMT: "decode_simt",
-             PA_LAUNCH_COMBINE: "combine", PA_LAUNCH_PREFILL_TC: "prefill_tc", PA_LAUNCH_GENERIC: "generic"}
+             PA_LAUNCH_COMBINE: "combine", PA_LAUNCH_PREFILL_TC: "prefill_tc", PA_LAUNCH_GENERIC: "generic",
+             PA_LAUNCH_PREFILL_PAIR: "prefill_pair"}
     return {n for bit, n in names.items() if mask & bit}
 
 

@@ -106,7 +106,7 @@ def step_metadata_for(query, k_pool, block_tables, context_lens, query_lens) -> 
     return StepMetadata.build(context_lens, query_lens, block_tables, num_tokens=query.shape[0],
                               pool_num_blocks=num_blocks, block_size=block_size, num_kv_heads=kv_heads,
                               device=query.device,
-                              prefill_tile_tokens=prefill_tile_tokens(query.shape[1], kv_heads))
+                              prefill_tile_tokens=prefill_tile_tokens(query.shape[1], kv_heads, query.shape[2]))
 
 
 def paged_attention_cuda(query, k_pool, v_pool, block_tables, context_lens, query_lens, scale):

@@ -243,11 +243,16 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
       g_last_launches |= PA_LAUNCH_COMBINE;
     }
   }
-  // Prefill rows go to the tcgen05 kernel when the plan was tiled for this head shape
-  // (128 / G query tokens per tile) and query/out rows are 16-byte aligned.
+  // Prefill rows go to a tcgen05 kernel when the plan's tiles fit one (256 rows = 256 / G
+  // query tokens: the CTA-pair kernel at head_dim 128; 128 rows: the single-CTA kernel)
+  // and query/out rows are 16-byte aligned.
   const int es = elem_size(dtype);
-  const bool tc_prefill = plan->num_prefill_tiles > 0 && prefill_tc_supported(dtype, head_dim, group, block_size) &&
-                          plan->prefill_tile_tokens * group == prefill_tile_rows() && q_stride_dim == 1 &&
+  const int tile_rows = plan->prefill_tile_tokens * group;
+  const bool pair_prefill = prefill_pair_supported(dtype, head_dim, group, block_size) &&
+                            tile_rows == prefill_pair_tile_rows();
+  const bool single_prefill = prefill_tc_supported(dtype, head_dim, group, block_size) &&
+                              tile_rows == prefill_tile_rows();
+  const bool tc_prefill = plan->num_prefill_tiles > 0 && (pair_prefill || single_prefill) && q_stride_dim == 1 &&
                           (q_stride_token * es) % 16 == 0 && (q_stride_head * es) % 16 == 0 &&
                           reinterpret_cast<uintptr_t>(query) % 16 == 0 && (out_stride_token * es) % 16 == 0 &&
                           (out_stride_head * es) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
@@ -278,9 +283,10 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
     f.pool_blocks = int32_t(pool_num_blocks);
     f.qscale = qscale;
     f.err = err;
-    cudaError_t e = launch_prefill_tc(dtype, head_dim, group, tk, tv, f, stream);
+    cudaError_t e = pair_prefill ? launch_prefill_pair(dtype, group, tk, tv, f, stream)
+                                 : launch_prefill_tc(dtype, head_dim, group, tk, tv, f, stream);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 prefill launch");
-    g_last_launches |= PA_LAUNCH_PREFILL_TC;
+    g_last_launches |= pair_prefill ? PA_LAUNCH_PREFILL_PAIR : PA_LAUNCH_PREFILL_TC;
   }
   const bool decode_left = plan->num_decode_seqs > 0 && !fast_decode;
   const bool prefill_left = plan->num_prefill_tokens > 0 && !tc_prefill;
@@ -408,7 +414,10 @@ int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t nu
                     num_blocks, staging, error_word, stream, "scatter_blocks");
 }
 
-int32_t pa_prefill_tile_rows(void) { return pa::prefill_tile_rows(); }
+int32_t pa_prefill_tile_rows(int32_t head_dim) {
+  (void)head_dim;  // the single-CTA kernel serves every head_dim by default (the pair kernel measured slower)
+  return pa::prefill_tile_rows();
+}
 
 int32_t pa_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
   using namespace pa;

@@ -165,6 +165,12 @@ bool prefill_tc_supported(int dtype, int head_dim, int group, int block_size);
 int prefill_tile_rows();
 cudaError_t launch_prefill_tc(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
                               const PrefillParams& p, cudaStream_t stream);
+// tcgen05 prefill on CTA pairs (cta_group::2, head_dim 128): tiles of
+// prefill_pair_tile_rows() rows, one cluster of two CTAs per tile and KV head.
+bool prefill_pair_supported(int dtype, int head_dim, int group, int block_size);
+int prefill_pair_tile_rows();
+cudaError_t launch_prefill_pair(int dtype, int group, const CUtensorMap& tk, const CUtensorMap& tv,
+                                const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);

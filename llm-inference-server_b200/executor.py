@@ -102,10 +102,10 @@ class CudaPagedExecutor:
         self.device = torch.device(device) if device is not None else pool.k[0].device
         if self.device.type != "cuda":
             raise NotImplementedError(f"ATTENTION=cuda: the paged executor needs a CUDA device, got {self.device}")
-        self.num_blocks, self.block_size, self.num_kv_heads, _ = pool.k[0].shape
+        self.num_blocks, self.block_size, self.num_kv_heads, head_dim = pool.k[0].shape
         cfg = model.config
         heads = getattr(cfg, "num_attention_heads", None) or cfg.n_head
-        self.tile_tokens = prefill_tile_tokens(heads, self.num_kv_heads)
+        self.tile_tokens = prefill_tile_tokens(heads, self.num_kv_heads, head_dim)
 
     @torch.inference_mode()
     def execute(self, seqs) -> list[int]:

@@ -29,20 +29,19 @@ def _as_i64(x) -> np.ndarray:
 
 _SM_COUNT: dict[int, int] = {}
 
-#: Rows of one tcgen05 prefill tile: (query token, GQA head) pairs.
-def prefill_tile_rows() -> int:
-    """(token, query-head) rows of one tensor-core prefill tile, as the loaded library's
-    kernel is built."""
-    return int(_lib.lib().pa_prefill_tile_rows())
+def prefill_tile_rows(head_dim: int = 128) -> int:
+    """(token, query-head) rows of one tensor-core prefill tile at this head_dim, as the
+    loaded library's kernels are built (256 for the CTA-pair kernel at head_dim 128)."""
+    return int(_lib.lib().pa_prefill_tile_rows(int(head_dim)))
 
 
-def prefill_tile_tokens(num_heads: int, num_kv_heads: int) -> int:
+def prefill_tile_tokens(num_heads: int, num_kv_heads: int, head_dim: int = 128) -> int:
     """Query tokens per prefill tile (the kernel's rows / G heads per KV head), or 0 when
     the group size has no tensor-core prefill instantiation (the generic kernel runs)."""
     if num_kv_heads <= 0 or num_heads % num_kv_heads:
         return 0
     g = num_heads // num_kv_heads
-    return prefill_tile_rows() // g if g in (1, 2, 4, 8) else 0
+    return prefill_tile_rows(head_dim) // g if g in (1, 2, 4, 8) else 0
 
 
 def sm_count(device: torch.device | None) -> int:

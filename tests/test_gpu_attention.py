@@ -22,6 +22,12 @@ NAME = {v: k for k, v in DT.items()}
 DEV = "cuda"
 
 
+def _pf(d: int) -> str:
+    """The tcgen05 prefill kernel a default plan runs at this head_dim (the single-CTA
+    kernel; the CTA-pair kernel runs for plans tiled at 256 rows)."""
+    return "prefill_tc"
+
+
 def _close(got: np.ndarray, ref: np.ndarray, dt: str, what: str = ""):
     np.testing.assert_allclose(got, ref, err_msg=what, **TOL[dt])
 
@@ -208,7 +214,7 @@ def test_tensor_core_prefill_matches_oracle(pkg, oracle, dtype, heads, kv_heads,
     qd = q.to(DEV)
     args = (kp.to(DEV), vp.to(DEV), bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
     tc = pkg.paged_attention_cuda(qd, *args).float().cpu().numpy()
-    assert {"prefill_tc", "decode_mma"} <= pkg._lib.last_launches() <= {"prefill_tc", "decode_mma", "combine"}
+    assert {_pf(d), "decode_mma"} <= pkg._lib.last_launches() <= {_pf(d), "decode_mma", "combine"}
     odd = torch.empty(q.shape[0], q.shape[1], d + 1, dtype=qd.dtype, device=DEV)[:, :, :d]
     odd.copy_(qd)
     generic = pkg.paged_attention_cuda(odd, *args).float().cpu().numpy()
@@ -262,4 +268,121 @@ def test_shared_prefix_blocks_match_oracle(pkg, oracle):
     ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), tables.numpy(),
                                         cl.numpy(), ql.numpy(), d ** -0.5, "bf16")
     _close(out, ref, "bf16", "shared prefix blocks")
+    assert pkg.read_device_error() == 0
+
+
+def _with_tiles(pkg, bt, cl, ql, num_tokens, nb, kv_heads, tile_tokens):
+    """Device block tables carrying a plan tiled at `tile_tokens` query tokens per prefill
+    tile (256 / G: the CTA-pair kernel; 128 / G: the single-CTA kernel)."""
+    meta = pkg.StepMetadata.build(cl, ql, bt, num_tokens=num_tokens, pool_num_blocks=nb, block_size=16,
+                                  num_kv_heads=kv_heads, device=DEV, prefill_tile_tokens=tile_tokens)
+    return pkg.attach(bt.to(DEV), meta)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("heads,kv_heads", [(16, 16), (16, 8), (32, 8), (64, 8)])
+def test_pair_prefill_matches_single_cta_kernel_and_oracle(pkg, oracle, dtype, heads, kv_heads):
+    """The CTA-pair prefill (256-row tiles over two SMs, each CTA holding half of every K/V
+    tile) against the single-CTA tcgen05 kernel on the same batch and the oracle, for GQA
+    groups 1/2/4/8 at head_dim 128: tiles whose second CTA has few or no tokens, prompts
+    shorter than one pair, prefix hits, contexts ending mid-block and mid-KV-tile."""
+    g = heads // kv_heads
+    lengths = PREFILL_LENGTHS + [(256 // g + 1, 256 // g + 1), (128 // g, 128 // g), (128 // g + 3, 128 // g + 3),
+                                 (1000, 256 // g), (333, 128 // g - 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=heads, kv_heads=kv_heads, dtype=DT[dtype],
+                                         seed=21)
+    qd, kd, vd = q.to(DEV), kp.to(DEV), vp.to(DEV)
+    cld, qld = cl.to(DEV), ql.to(DEV)
+    pair_bt = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, 256 // g)
+    pair = pkg.paged_attention_cuda(qd, kd, vd, pair_bt, cld, qld, 128 ** -0.5).float().cpu().numpy()
+    assert "prefill_pair" in pkg._lib.last_launches() and "prefill_tc" not in pkg._lib.last_launches()
+    single_bt = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, 128 // g)
+    single = pkg.paged_attention_cuda(qd, kd, vd, single_bt, cld, qld, 128 ** -0.5).float().cpu().numpy()
+    assert "prefill_tc" in pkg._lib.last_launches() and "prefill_pair" not in pkg._lib.last_launches()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), 128 ** -0.5, dtype)
+    _close(pair, ref, dtype, "CTA-pair prefill")
+    _close(single, ref, dtype, "single-CTA prefill")
+    np.testing.assert_allclose(pair, single, atol=1e-2, rtol=1e-2)
+    assert pkg.read_device_error() == 0
+
+
+@pytest.mark.parametrize("tiles", ["pair", "single"])
+def test_prefill_ignores_stale_rows_past_the_context(pkg, oracle, tiles):
+    """The reference slices every sequence's keys to its context (attention.py:171-172),
+    so whatever a freed-and-reused block holds past the context never reaches it.  Fill
+    those rows of K and V with NaN: the tcgen05 kernels must give the oracle's result."""
+    lengths = [(70, 70), (100, 37), (17, 17), (1000, 999), (130, 130)]
+    heads, kv_heads = 32, 8
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=heads, kv_heads=kv_heads,
+                                         dtype=torch.bfloat16, seed=8)
+    kp_bad, vp_bad = kp.clone(), vp.clone()
+    for i, (c, _) in enumerate(lengths):
+        last = int(bt[i, (c - 1) // 16])
+        kp_bad[last, c % 16 or 16:] = float("nan")
+        vp_bad[last, c % 16 or 16:] = float("nan")
+    tile = (256 if tiles == "pair" else 128) // (heads // kv_heads)
+    btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, tile)
+    out = pkg.paged_attention_cuda(q.to(DEV), kp_bad.to(DEV), vp_bad.to(DEV), btd, cl.to(DEV), ql.to(DEV),
+                                   128 ** -0.5).float().cpu().numpy()
+    assert ("prefill_pair" if tiles == "pair" else "prefill_tc") in pkg._lib.last_launches()
+    assert np.isfinite(out).all()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), 128 ** -0.5, "bf16")
+    _close(out, ref, "bf16", f"{tiles} prefill with NaN past the context")
+
+
+def _torch_gather_reference(q, kp, vp, bt, cl, ql, scale, rows=512):
+    """The reference gather path's arithmetic on the GPU, for sizes the numpy oracle is too
+    slow for, with the oracle's rounding points (attention.py:156-187): products computed
+    in float32 and rounded to the pool dtype (the reference's half-precision matmuls
+    return that dtype), the scaled scores rounded, softmax in float32, probabilities
+    rounded before P.V, the output rounded.  Pinned against the oracle on a small case in
+    the test that uses it."""
+    def rnd(x):
+        return x.to(vp.dtype).float()
+
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    heads, bs, kvh = q.shape[1], kp.shape[1], kp.shape[2]
+    start = 0
+    for i in range(bt.shape[0]):
+        c, n = int(cl[i]), int(ql[i])
+        blocks = bt[i, :(c + bs - 1) // bs].to(q.device)
+        k = kp[blocks].flatten(0, 1)[:c].float().repeat_interleave(heads // kvh, dim=1).transpose(0, 1)
+        v = vp[blocks].flatten(0, 1)[:c].float().repeat_interleave(heads // kvh, dim=1).transpose(0, 1)
+        for r0 in range(0, n, rows):
+            r1 = min(n, r0 + rows)
+            qq = q[start + r0:start + r1].float().transpose(0, 1)
+            s = rnd(rnd(torch.matmul(qq, k.transpose(-1, -2))) * scale)
+            qpos = torch.arange(c - n + r0, c - n + r1, device=q.device)
+            s = s.masked_fill(torch.arange(c, device=q.device)[None, :] > qpos[:, None], float("-inf"))
+            p = rnd(torch.softmax(s, dim=-1, dtype=torch.float32))
+            out[start + r0:start + r1] = rnd(torch.matmul(p, v)).transpose(0, 1)
+        start += n
+    return out
+
+
+def test_long_context_prefill_matches_reference(pkg, oracle):
+    """Long rows of the tcgen05 prefill at the Llama-8B shape: a 4,600-token prompt and a
+    prefix-cache hit of 700 new tokens over a 9,300-token context (plus a decode row),
+    every row compared with the gather arithmetic in torch float32.  That torch reference
+    is itself pinned to the oracle on a small batch first."""
+    heads, kv_heads, d = 32, 8, 128
+    small = [(300, 300), (200, 57), (90, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch(small, bs=16, d=d, heads=heads, kv_heads=kv_heads, dtype=torch.bfloat16,
+                                         seed=2)
+    mine = _torch_gather_reference(q.to(DEV), kp.to(DEV), vp.to(DEV), bt, cl, ql, d ** -0.5, rows=64).cpu().numpy()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), d ** -0.5, "bf16")
+    np.testing.assert_allclose(mine, ref, atol=1e-2, rtol=1e-2)
+
+    lengths = [(4600, 4600), (9300, 700), (12000, 1)]
+    q, kp, vp, bt, cl, ql = ragged_batch_device(lengths, bs=16, d=d, heads=heads, kv_heads=kv_heads,
+                                                dtype=torch.bfloat16, device=DEV, seed=6)
+    ref = _torch_gather_reference(q, kp, vp, bt, cl, ql, d ** -0.5).cpu().numpy()
+    for rows, kernel in ((128, "prefill_tc"), (256, "prefill_pair")):
+        btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, rows // (heads // kv_heads))
+        out = pkg.paged_attention_cuda(q, kp, vp, btd, cl.to(DEV), ql.to(DEV), d ** -0.5)
+        assert {kernel, "decode_mma"} <= pkg._lib.last_launches()
+        _close(out.float().cpu().numpy(), ref, "bf16", f"long-context prefill ({kernel})")
     assert pkg.read_device_error() == 0

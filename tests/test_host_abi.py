@@ -279,7 +279,10 @@ def test_multi_gpu_and_block_entry_points_reject_bad_arguments(pkg):
         pkg._lib.check(lib.pa_ipc_export(None, None, None))
     with pytest.raises(ValueError):
         pkg._lib.check(lib.pa_ipc_open(None, 0, None))
-    assert pkg.metadata.prefill_tile_rows() == lib.pa_prefill_tile_rows() > 0
+    # default plans use the single-CTA kernel's 128-row tiles at every head_dim
+    assert pkg.metadata.prefill_tile_rows(128) == lib.pa_prefill_tile_rows(128) == 128
+    assert pkg.metadata.prefill_tile_rows(64) == lib.pa_prefill_tile_rows(64) == 128
+    assert pkg.metadata.prefill_tile_tokens(32, 8, 128) == 32 and pkg.metadata.prefill_tile_tokens(12, 12, 64) == 128
 
 
 def test_fused_oproj_allreduce_rejects_bad_arguments(pkg):

@@ -56,7 +56,7 @@ def _case(pkg, lengths, dtype, heads, kv_heads, d, seed):
     ref = pkg.paged_attention_cuda(q, kp, vp, bt.to(DEV), cl.to(DEV), ql.to(DEV), scale)
     meta = pkg.StepMetadata.build(cl, ql, bt, num_tokens=q.shape[0], pool_num_blocks=kp.shape[0], block_size=16,
                                   num_kv_heads=kv_heads, device=DEV,
-                                  prefill_tile_tokens=pkg.prefill_tile_tokens(heads, kv_heads))
+                                  prefill_tile_tokens=pkg.prefill_tile_tokens(heads, kv_heads, d))
     return q, kp, vp, meta, scale, ref
 
 
