@@ -225,9 +225,12 @@ class ClockSampler:
         pw = [p for p in power if p is not None]
         loaded = [s for s, p in zip(sm, power) if s is not None and p is not None and pw and p > 0.5 * max(pw)]
         sm_ok = [s for s in sm if s is not None]
+        capped = sum(1 for r in rows if r[8].lower().startswith("active"))
         return {"sm_mhz": statistics.median(loaded or sm_ok) if sm_ok else None,
                 "sm_max_mhz": max([m for m in mx if m is not None], default=None),
-                "reasons": sorted(reasons), "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "reasons": sorted(reasons), "samples": len(rows), "power_w_max": max(pw) if pw else None,
+                "sm_mhz_min": min(loaded or sm_ok) if sm_ok else None,
+                "sw_power_cap_frac": capped / len(rows)}
 
 
 # ------------------------------------------------------------------ CPU legs (oracle)
@@ -290,26 +293,194 @@ def _cpu_sample_text(wl: Workload, nseq: int, ctx, reps: int, dtype: str = "bf16
             f"{os.cpu_count()} CPUs")
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def _reference_modules():
+    """The unmodified reference server installed in ``baseline/_ref`` (by
+    ``baseline/install_reference.py``), or None when it is not installed.  Its modules
+    are imported as they are; ``DEVICE`` defaults to ``cpu`` for its config."""
+    if not (REF_DIR / "inference_server" / "core" / "attention.py").exists():
+        return None
+    import importlib
+    import types
+
+    os.environ.setdefault("DEVICE", "cpu")
+    if str(REF_DIR) not in sys.path:
+        sys.path.append(str(REF_DIR))
+    names = dict(config="config", attention="core.attention", paged_executor="core.paged_executor",
+                 kv_pool="core.kv_pool", block_allocator="core.block_allocator", scheduler="core.scheduler",
+                 sequence="core.sequence")
+    return types.SimpleNamespace(**{k: importlib.import_module(f"inference_server.{v}") for k, v in names.items()})
+
+
+class ReferenceStepSample:
+    """One layer of the reference's own step on the host CPU, on a bounded sample of the
+    workload, scaled to the whole step.
+
+    The sample runs, unchanged, the reference's KV append (``_PagedCache.update``,
+    inference_server/core/paged_executor.py:116-125) and gather attention
+    (``paged_attention_gather``, core/attention.py:92-187) on a ``PagedKVPool`` holding
+    one layer, in the workload's dtype, with ``torch.set_num_threads(os.cpu_count())``:
+
+    * decode: ``nseq`` sequences that include the batch's longest one.  The reference's
+      batched decode pads every row to the longest context of the batch
+      (core/attention.py:130-153), so the full batch costs ``batch / nseq`` times the
+      sample;
+    * prefill (workloads with churn): the first ``npf`` churn prompts of step 0 through
+      the per-sequence ragged loop (core/attention.py:156-187), whose dense scores cost
+      grows with prompt length squared; scaled by the step's sum of squared prompt
+      lengths over the sample's.
+
+    ``step_seconds = layers * (t_decode * batch / nseq + t_prefill * prefill_scale)`` and
+    the value is the step's generated tokens (batch + churn prompts) over that.
+    """
+
+    def __init__(self, ref, wl: "Workload", nseq: int, npf: int, dtype: str, seed: int = 1234):
+        self.ref, self.wl = ref, wl
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cores = torch.get_num_threads()
+        tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+        g = torch.Generator().manual_seed(seed)
+        bs, Hq, Hkv, D = wl.block_size, wl.heads, wl.kv_heads, wl.head_dim
+        ctx_all = wl.context_lens(0)
+        longest = int(np.argmax(ctx_all))
+        sel = [longest] + [i for i in range(wl.batch) if i != longest][:max(nseq, 1) - 1]
+        self.ctx = ctx_all[sel].astype(np.int64)
+        self.plen = wl.prompt_lens(0)[:npf].astype(np.int64) if wl.n_churn and npf else np.zeros(0, np.int64)
+        need_d, need_p = -(-self.ctx // bs), -(-self.plen // bs)
+        nb = int(need_d.sum() + need_p.sum()) + 1
+        dims = ref.kv_pool.ModelDims(num_layers=1, num_kv_heads=Hkv, head_dim=D, dtype=tdt)
+        self.pool = ref.kv_pool.PagedKVPool(dims, num_blocks=nb, block_size=bs, device="cpu")
+        self.pool.k[0].copy_(torch.randn(self.pool.k[0].shape, generator=g))
+        self.pool.v[0].copy_(torch.randn(self.pool.v[0].shape, generator=g))
+        perm = torch.randperm(nb, generator=g).tolist()
+
+        def layout(lens, q_lens):
+            nonlocal perm
+            rows, slots = [], []
+            for c, q in zip(lens.tolist(), q_lens.tolist()):
+                n = -(-c // bs)
+                blocks, perm = perm[:n], perm[n:]
+                rows.append(blocks)
+                slots += [blocks[p // bs] * bs + p % bs for p in range(c - q, c)]
+            width = max(len(r) for r in rows)
+            tables = torch.tensor([r + [0] * (width - len(r)) for r in rows], dtype=torch.long)
+            return tables, torch.tensor(slots, dtype=torch.long)
+
+        def case(lens, q_lens):
+            tables, slots = layout(lens, q_lens)
+            t = int(q_lens.sum())
+            return dict(q=torch.randn(t, Hq, D, generator=g).to(tdt),
+                        k=torch.randn(1, Hkv, t, D, generator=g).to(tdt), v=torch.randn(1, Hkv, t, D, generator=g).to(tdt),
+                        tables=tables, slots=slots, ctx=torch.from_numpy(lens), ql=torch.from_numpy(q_lens))
+
+        self.decode = case(self.ctx, np.ones_like(self.ctx))
+        self.prefill = case(self.plen, self.plen) if len(self.plen) else None
+        self.scale = D ** -0.5
+        full_sq = float(np.sum(wl.prompt_lens(0).astype(np.float64) ** 2)) if wl.n_churn else 0.0
+        self.pf_scale = full_sq / float(np.sum(self.plen.astype(np.float64) ** 2)) if len(self.plen) else 0.0
+        self.dec_scale = wl.batch / len(self.ctx)
+        self.last = (0.0, 0.0)
+
+    def _layer(self, c) -> float:
+        pe, attention = self.ref.paged_executor, self.ref.attention
+        t0 = time.perf_counter()
+        sc = pe._StepContext(write_slots=c["slots"], block_tables=c["tables"], context_lens=c["ctx"],
+                             query_lens=c["ql"], pool=self.pool)
+        pe._PagedCache(sc).update(c["k"], c["v"], 0)
+        attention.paged_attention_gather(c["q"], self.pool.k[0], self.pool.v[0], c["tables"], c["ctx"], c["ql"],
+                                         self.scale)
+        return time.perf_counter() - t0
+
+    def step_seconds(self) -> float:
+        """Runs the sample once; returns the scaled seconds of one whole step."""
+        t_dec = self._layer(self.decode)
+        t_pf = self._layer(self.prefill) if self.prefill is not None else 0.0
+        self.last = (t_dec, t_pf)
+        return self.wl.layers * (t_dec * self.dec_scale + t_pf * self.pf_scale)
+
+    @property
+    def tokens_per_step(self) -> int:
+        return self.wl.batch + self.wl.n_churn
+
+    def describe(self, reps: int) -> str:
+        pf = (f"; prefill: churn prompts {self.plen.tolist()} through the ragged loop, scaled x{self.pf_scale:.2f} "
+              f"(sum of squared prompt lengths) to the step's {self.wl.n_churn} prompts") if len(self.plen) else ""
+        return (f"the reference's own _PagedCache.update + paged_attention_gather (baseline/_ref, unchanged) on "
+                f"one layer, {str(self.pool.k[0].dtype).replace('torch.', '')}, torch CPU with "
+                f"{self.cores} threads; decode: {len(self.ctx)} sequences incl. the batch's longest (contexts "
+                f"{self.ctx.tolist()}), padded rows scaled x{self.dec_scale:.0f} to the batch of {self.wl.batch}"
+                f"{pf}; x{self.wl.layers} layers; {reps} repetitions; last decode/prefill layer "
+                f"{self.last[0] * 1e3:.0f}/{self.last[1] * 1e3:.0f} ms; host has {os.cpu_count()} CPUs")
+
+
+def _cpu_leg(args, wl: "Workload", dtype: str) -> dict | None:
+    """The CPU baseline beside the GPU line: the reference's own code when it is
+    installed (``kind: reference``), else the numpy port (``kind: port``)."""
+    ref = _reference_modules()
+    if ref is not None:
+        s = ReferenceStepSample(ref, wl, args.cpu_sample_seqs, args.cpu_sample_prompts, dtype)
+        s.step_seconds()                                           # warm-up
+        t_end = time.perf_counter() + args.cpu_budget_s
+        reps = []
+        while len(reps) < 2 or time.perf_counter() < t_end:
+            reps.append(s.step_seconds())
+        return {"value": s.tokens_per_step / float(np.mean(reps)), "unit": "tok/s", "cores": s.cores,
+                "kind": "reference", "sample": s.describe(len(reps))}
+    one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs, dtype)
+    one()
+    t_end = time.perf_counter() + args.cpu_budget_s
+    reps = []
+    while len(reps) < 2 or time.perf_counter() < t_end:
+        reps.append(one())
+    return {"value": args.cpu_sample_seqs / (float(np.mean(reps)) * wl.layers), "unit": "tok/s",
+            "cores": _blas_threads(), "kind": "port",
+            "sample": "reference not installed in baseline/_ref; " + _cpu_sample_text(wl, args.cpu_sample_seqs, ctx,
+                                                                                      len(reps), dtype)}
+
+
 def run_reference(args, rank: int, world: int) -> None:
-    """`--impl reference`: the reference algorithm's CPU port, rank 0 only."""
+    """``--impl reference``: the reference's own CPU path on this host's cores, rank 0
+    only.  Attention workloads time ``ReferenceStepSample`` (each step = one run of the
+    sample, scaled to a whole step); ``config1`` serves a bounded sample of its requests
+    through the reference's Scheduler + PagedExecutor.  Falls back to the numpy port,
+    saying so in ``kind``, when the reference is not installed."""
     if rank != 0:
         return
-    wl = _make_workload(args, rank, max_steps=1)
-    nseq = args.cpu_sample_seqs
     dt = WORKLOADS[args.workload]["dtype"]
-    one, ctx = _oracle_layer_timer(wl, nseq, dt)
-    for _ in range(args.warmup):
-        one()
-    times = [one() for _ in range(args.steps)]
-    sec_layer = float(np.mean(times))
-    value = nseq / (sec_layer * wl.layers)
+    if args.workload == "config1":
+        cpu = _c1_cpu_sample(args)
+        value, ms, wl_cfg = cpu["value"], None, {"workload": "BASELINE config 1 (see the GPU line)",
+                                                "model": "gpt2-124m (random-init)"}
+        steps, sample = 1, cpu
+    else:
+        wl = _make_workload(args, rank, max_steps=1)
+        ref = _reference_modules()
+        if ref is not None:
+            s = ReferenceStepSample(ref, wl, args.cpu_sample_seqs, args.cpu_sample_prompts, dt)
+            for _ in range(args.warmup):
+                s.step_seconds()
+            times = [s.step_seconds() for _ in range(args.steps)]
+            value = s.tokens_per_step / float(np.mean(times))
+            sample = {"value": value, "unit": "tok/s", "cores": s.cores, "kind": "reference",
+                      "sample": s.describe(len(times))}
+        else:
+            one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs, dt)
+            for _ in range(args.warmup):
+                one()
+            times = [one() * wl.layers * wl.batch / args.cpu_sample_seqs for _ in range(args.steps)]
+            value = wl.batch / float(np.mean(times))
+            sample = {"value": value, "unit": "tok/s", "cores": _blas_threads(), "kind": "port",
+                      "sample": "reference not installed in baseline/_ref; " +
+                                _cpu_sample_text(wl, args.cpu_sample_seqs, ctx, len(times), dt)}
+        ms, wl_cfg, steps = float(np.mean(times)) * 1e3, _config(args, wl, world), args.steps
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_layer * 1e3, "higher_is_better": True,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic",
-        "config": _config(args, wl, world),
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": _blas_threads(), "kind": "port",
-                         "sample": _cpu_sample_text(wl, nseq, ctx, len(times), dt)},
+        "config": wl_cfg,
+        "cpu_baseline": sample,
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "host_cpus": os.cpu_count(),
     }
@@ -968,23 +1139,58 @@ def run_engine(args, rank: int, world: int, local_rank: int) -> None:
 
 
 def _c1_cpu_sample(args) -> dict:
-    """The reference executor's algorithm on the host CPU (the oracle's append and gather
-    attention under the same GPT-2), on a bounded sample of config 1's requests."""
-    sys.path.insert(0, str(ROOT / "tests"))
+    """BASELINE config 1 on the host CPU through the reference's own engine parts: its
+    ``Scheduler`` (admission, prefill-priority selection, growth), ``BlockAllocator``,
+    ``PagedKVPool`` and ``PagedExecutor`` with ``ATTENTION=gather`` on ``DEVICE=cpu``,
+    all imported unchanged from ``baseline/_ref``, serving a bounded sample of the 200
+    requests (the first 8, at concurrency 4) with a random-init GPT-2 (seed 0, fp32).
+    Falls back to the oracle port under the bench's own loop when the reference is not
+    installed."""
     from transformers import GPT2Config, GPT2LMHeadModel
 
-    from _engine import OracleExecutor
-
+    torch.set_num_threads(os.cpu_count() or 1)
     torch.manual_seed(0)
     model = GPT2LMHeadModel(GPT2Config()).eval()
-    ex = OracleExecutor(model, 12, 2048, 16, 12, 64)
-    sample = _c1_requests(200, args.seed)[:4]
-    t = time.perf_counter()
-    gen, passes = _serve(ex, sample, 4, 2048)
-    dt = time.perf_counter() - t
-    return {"value": gen / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"the first 4 of the 200 requests at concurrency 4 ({gen} tokens, {passes} passes): GPT-2 on "
-                      "the host CPU with the oracle's KV append and gather-path attention"}
+    sample = _c1_requests(200, args.seed)[:8]
+    ref = _reference_modules()
+    if ref is None:
+        sys.path.insert(0, str(ROOT / "tests"))
+        from _engine import OracleExecutor
+
+        ex = OracleExecutor(model, 12, 2048, 16, 12, 64)
+        t = time.perf_counter()
+        gen, passes = _serve(ex, sample[:4], 4, 2048)
+        dt = time.perf_counter() - t
+        return {"value": gen / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"reference not installed in baseline/_ref; the first 4 of the 200 requests at concurrency "
+                          f"4 ({gen} tokens, {passes} passes): GPT-2 on the host CPU with the oracle's KV append and "
+                          "gather-path attention"}
+    C = ref.config.CONFIG
+    saved = {k: getattr(C, k) for k in ("device", "attention", "max_running", "block_size", "prefix_caching")}
+    try:
+        C.device, C.attention, C.max_running, C.block_size, C.prefix_caching = "cpu", "gather", 4, 16, False
+        pool = ref.kv_pool.PagedKVPool.from_model(model, num_blocks=2048, block_size=16, device="cpu")
+        ex = ref.paged_executor.PagedExecutor(model, None, pool)
+        alloc = ref.block_allocator.BlockAllocator(2048)
+        sched = ref.scheduler.Scheduler(ex, -1, allocator=alloc, pool=pool)
+        seqs = [ref.sequence.Sequence(seq_id=f"r{i}", prompt_token_ids=p, max_tokens=o)
+                for i, (p, o) in enumerate(sample)]
+        for q in seqs:
+            sched.add(q)
+        t = time.perf_counter()
+        passes = 0
+        while sched.has_work:
+            sched.step()
+            passes += 1
+        dt = time.perf_counter() - t
+    finally:
+        for k, v in saved.items():
+            setattr(C, k, v)
+    gen = sum(len(q.output_token_ids) for q in seqs)
+    return {"value": gen / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"the reference's Scheduler + PagedExecutor (ATTENTION=gather, DEVICE=cpu; baseline/_ref, "
+                      f"unchanged) serving the first 8 of the 200 requests at concurrency 4 ({gen} tokens, {passes} "
+                      f"passes, {dt:.1f} s) with GPT-2 random-init fp32 on {torch.get_num_threads()} threads"}
 
 
 BLOCK_POOL_BLOCKS = 16384   # per layer: 16384 x [16, 8, 128] bf16 = 512 MB for K and V
@@ -1403,19 +1609,34 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         e2e_ms = e_start.elapsed_time(e_end)
     assert pkg.read_device_error(dev) == 0, "a kernel set the device error word"
 
-    # ---- max over ranks
-    times = torch.tensor([elapsed_ms, e2e_ms, float(np.mean(dec_ms)), float(np.mean(pre_ms))],
-                         dtype=torch.float64, device=dev)
+    # ---- max over ranks, plus every rank's own figures (a slow rank vs a power-capped node)
+    timed = [args.warmup + k for k in range(args.steps)]
+    csum = clocks.summary()
+    my_dec_gbs = float(np.mean([wl.attention_bytes(s, elem) for s in timed])) / (float(np.mean(dec_ms)) / 1e3) / 1e9
+    my_pre_tflops = (float(np.mean([wl.prefill_flops(s) for s in timed])) / (float(np.mean(pre_ms)) / 1e3) / 1e12
+                     if wl.n_churn else 0.0)
+    mine = torch.tensor([elapsed_ms, e2e_ms, float(np.mean(dec_ms)), float(np.mean(pre_ms)), my_dec_gbs, my_pre_tflops,
+                         float(csum.get("sm_mhz") or 0.0), float(csum.get("sw_power_cap_frac") or 0.0),
+                         float(csum.get("power_w_max") or 0.0)], dtype=torch.float64, device=dev)
     if world > 1:
-        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, dec_avg_ms, pre_avg_ms = times.tolist()
+        every = torch.empty(world, mine.numel(), dtype=torch.float64, device=dev)
+        torch.distributed.all_gather_into_tensor(every, mine)
+    else:
+        every = mine[None]
+    every = every.cpu().numpy()
+    elapsed_ms, e2e_ms, dec_avg_ms, pre_avg_ms = (float(x) for x in every[:, :4].max(axis=0))
     if rank != 0:
         return
+    per_rank = {"step_ms": [round(float(x) / args.steps, 3) for x in every[:, 0]],
+                "decode_gbs": [round(float(x), 1) for x in every[:, 4]],
+                "prefill_tflops": [round(float(x), 1) for x in every[:, 5]] if wl.n_churn else None,
+                "sm_mhz_median": [float(x) for x in every[:, 6]],
+                "sw_power_cap_frac": [round(float(x), 3) for x in every[:, 7]],
+                "power_w_max": [round(float(x), 1) for x in every[:, 8]]}
 
     tokens = (B + wl.n_churn) * args.steps * world
     value = tokens / (elapsed_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
-    timed = [args.warmup + k for k in range(args.steps)]
     bytes_per_call = float(np.mean([wl.attention_bytes(s, elem) for s in timed]))
     achieved = bytes_per_call / (dec_avg_ms / 1e3) / 1e9
     hbm_peak, bf16_peak, peak_kind = _measured_peaks()
@@ -1425,15 +1646,8 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     pre_tflops = pre_flops / (pre_avg_ms / 1e3) / 1e12 if wl.n_churn else None
 
     cpu = None
-    if world == 1 and not args.no_cpu_baseline and args.workload == "config3":
-        one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs)
-        one()
-        t_end = time.perf_counter() + args.cpu_budget_s
-        reps = []
-        while len(reps) < 2 or time.perf_counter() < t_end:
-            reps.append(one())
-        cpu = {"value": args.cpu_sample_seqs / (float(np.mean(reps)) * L), "unit": "tok/s", "cores": _blas_threads(),
-               "kind": "port", "sample": _cpu_sample_text(wl, args.cpu_sample_seqs, ctx, len(reps))}
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_leg(args, wl, "f32" if f32 else "bf16")
 
     # rank 0's per-launch spread (CUDA events per layer): shows a bimodal launch population
     def pct(xs, digits):
@@ -1473,7 +1687,8 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(np.mean(h2d_bytes)),
                 "d2h_bytes_per_step": int(np.mean(d2h_bytes)), "ms_per_step": e2e_ms / args.steps},
         "gpu_launches": gpu_launches,
-        "clocks": clocks.summary(),
+        "clocks": csum,
+        "per_rank": per_rank,
         "decode_splits": {"split_blocks": metas_d[0].plan.split_blocks, "items": metas_d[0].plan.num_decode_items,
                           "combine_seqs": metas_d[0].plan.num_combine_seqs},
     }
@@ -1510,7 +1725,9 @@ def main() -> None:
                     help="config3 (default headline), BASELINE config 2's isolated decode microbenchmark, "
                          "config5 (70B shape, KV heads sharded over --gpus), or blocks (copy-on-write and swap "
                          "moves)")
-    ap.add_argument("--cpu-sample-seqs", type=int, default=4)
+    ap.add_argument("--cpu-sample-seqs", type=int, default=4,
+                    help="decode sequences in the CPU baseline's sample (the batch's longest among them)")
+    ap.add_argument("--cpu-sample-prompts", type=int, default=2, help="churn prompts in the CPU baseline's sample")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graphs", action="store_true",
