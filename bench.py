@@ -501,6 +501,8 @@ WORKLOADS = {
     # (--gpus N = tensor-parallel size), o_proj row-split, one all-reduce per layer.
     "config5": dict(heads=64, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=8192.0, median_ctx=None,
                     lo=128, hi=32768, layers=80, churn=0.0, batch=512, d_model=8192),
+    "config5-decode": dict(heads=64, kv_heads=8, head_dim=128, dtype="bf16", mean_ctx=8192.0, median_ctx=None,
+                    lo=128, hi=32768, layers=80, churn=0.0, batch=512, d_model=8192),
     # the serving engine end to end, GPT-2 124M random-init, fp32.
     "config1": dict(heads=12, kv_heads=12, head_dim=64, dtype="f32", mean_ctx=0.0, median_ctx=None,
                     lo=0, hi=0, layers=12, churn=0.0, batch=32),
@@ -556,7 +558,7 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
            for _ in range(L)]
     bt = torch.from_numpy(wl.tables).to(dev)
     sm = pkg.metadata.sm_count(dev)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
+    tile = _prefill_tile(pkg, args, Hq, Hkv, D)
     dummy = torch.zeros(1, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -728,6 +730,382 @@ def run_tp(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+SERVE_POOL_FRACTION = 0.90     # config 5: the pool takes ~90 % of the HBM left after weights and buffers
+SERVE_MAX_PASS_TOKENS = 131072 # tokens one pass may feed (four 32k-token recomputes)
+SERVE_OPROJ_CHUNK = 16384      # prefill passes run o_proj + all-reduce in chunks of this many tokens
+
+
+def run_serve_tp(args, rank: int, world: int, local_rank: int) -> None:
+    """``--workload config5``: BASELINE config 5 served as stated — Llama-3-70B attention
+    shape (64 q / 8 kv heads, head_dim 128, bf16, 80 layers, d_model 8192), 512 requests
+    with contexts lognormal mean 8192 clipped 128..32768, KV heads sharded over the
+    ``--gpus N`` ranks with a row-split o_proj and one all-reduce per layer, and each
+    rank's 80-layer pool sized to ~90 % of the HBM left after the o_proj weights and the
+    pass buffers, so the batch is bounded by the pool and recompute preemption fires.
+
+    Scheduling is ``ServeSim`` (the reference scheduler's policy, checked step for step
+    against it on CPU): a pass is either the admitted sequences' prefill (whole history;
+    a preempted victim's recompute included) through the tcgen05 varlen prefill kernel,
+    or one decode token for every running sequence.  The run starts from a steady state:
+    requests are admitted in order while they fit, as if their prompts had been prefilled
+    (their KV resident, random); the rest wait.  Output lengths are lognormal with median
+    64 (sigma 0.9, clipped 1..512), borrowed from config 4 because config 5 states none.
+    Per pass and layer: fused K+V append, paged attention over the rank's heads, the
+    rank's o_proj row slice, all-reduce (decode: the peer-memory kernel; prefill: NCCL in
+    chunks of 16k tokens).  value = tokens sampled / time (both pass kinds sample one
+    token per sequence); the line splits the time by pass kind and by operation."""
+    import importlib
+
+    from __graft_entry__ import import_package
+
+    pkg = import_package()
+    tpm = importlib.import_module(f"{pkg.__name__}.tensor_parallel")
+    w = WORKLOADS["config5"]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if w["kv_heads"] % world:
+        raise SystemExit(f"config5 shards {w['kv_heads']} KV heads; {world} ranks do not divide them")
+    L, NREQ, D, DM, BS = args.layers, args.batch, w["head_dim"], w["d_model"], 16
+    qs, ks = tpm.kv_head_shard(w["heads"], w["kv_heads"], rank, world)
+    Hq, Hkv = qs.stop - qs.start, ks.stop - ks.start
+    rng = np.random.default_rng(args.seed)
+    mu = clipped_lognormal_mu(w["mean_ctx"], 0.9, w["lo"], w["hi"])
+    prompts = np.clip(np.exp(rng.normal(mu, 0.9, size=NREQ)), w["lo"], w["hi"]).astype(np.int64)
+    outs = np.clip(np.exp(rng.normal(np.log(64.0), 0.9, size=NREQ)), 1, 512).astype(np.int64)
+
+    # ---- weights and pass buffers first, then the pool from what is left
+    g = torch.Generator(device=dev).manual_seed(args.seed + 100 * rank)
+    w_o = [(torch.randn(Hq * D, DM, generator=g, device=dev) / (w["heads"] * D) ** 0.5).to(torch.bfloat16)
+           for _ in range(L)]
+    T = SERVE_MAX_PASS_TOKENS
+    q_buf = torch.randn(T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    k_new = torch.randn(T, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+    v_new = torch.randn(T, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+    proj = torch.empty(SERVE_OPROJ_CHUNK, DM, dtype=torch.bfloat16, device=dev)
+    reducer = (tpm.PeerAllReduce(NREQ * DM, torch.bfloat16, device=dev, timeout_s=10.0)
+               if world > 1 and args.allreduce == "peer" else None)
+    torch.cuda.synchronize(dev)
+    free_b, total_b = torch.cuda.mem_get_info(dev)
+    # the attention output of the largest pass is allocated per pass: keep room for it
+    budget = free_b - T * Hq * D * 2 - (2 << 30)
+    block_bytes = L * 2 * BS * Hkv * D * 2
+    nb = int(SERVE_POOL_FRACTION * budget // block_bytes)
+    shape = (nb, BS, Hkv, D)
+    k_pools = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    v_pools = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    for t in k_pools + v_pools:
+        t.normal_(generator=g)
+    pool_bytes = 2 * L * nb * BS * Hkv * D * 2
+
+    sim = ServeSim(nb, BS, max_running=NREQ)
+    seqs = [SimSeq(i, int(p), int(o)) for i, (p, o) in enumerate(zip(prompts, outs))]
+    resident = 0
+    for s in seqs:
+        if resident == len(sim.running) and sim.admit_resident(s):
+            resident += 1
+        else:
+            sim.add(s)
+    # the largest pass's attention output and a generous split-K workspace are cached
+    # before timing, so the timed passes allocate nothing new from the nearly full HBM
+    pkg.attention._workspace(dev, 64 << 20)
+    tmp = torch.empty(T * Hq * D, dtype=torch.bfloat16, device=dev)
+    del tmp
+    sm = pkg.metadata.sm_count(dev)
+    tile = _prefill_tile(pkg, args, Hq, Hkv, D)
+    dummy = torch.zeros(1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    launches = [0]
+
+    def plan(batch):
+        width = max(len(s.blocks) for s in batch)
+        tables = np.zeros((len(batch), width), dtype=np.int64)
+        for i, s in enumerate(batch):
+            tables[i, :len(s.blocks)] = s.blocks
+        ctx = np.array([s.after_next for s in batch], dtype=np.int64)
+        ql = np.array([s.feed for s in batch], dtype=np.int64)
+        meta = pkg.StepMetadata.plan_host(ctx, ql, tables, num_tokens=int(ql.sum()), pool_num_blocks=nb,
+                                          block_size=BS, num_kv_heads=Hkv, sm=sm, prefill_tile_tokens=tile,
+                                          pinned=True)
+        return meta, torch.from_numpy(tables).to(dev, non_blocking=True)
+
+    def run_pass(batch, marks):
+        meta, bt = plan(batch)
+        tokens = meta.num_tokens
+        if tokens > T:
+            raise SystemExit(f"config5: a pass feeds {tokens} tokens (> {T}); raise SERVE_MAX_PASS_TOKENS")
+        meta = meta.upload(dev)
+        slots = meta.slot_mapping()
+        bta = pkg.attach(bt, meta)
+        decode = not any(s.prefilling for s in batch)
+        for l in range(L):
+            marks[l][0].record(stream)
+            pkg.reshape_and_cache(k_new[:tokens], v_new[:tokens], k_pools[l], v_pools[l], slots)
+            attn = pkg.paged_attention_cuda(q_buf[:tokens], k_pools[l], v_pools[l], bta, dummy, dummy, D ** -0.5)
+            launches[0] += 1 + bin(pkg._lib.lib().pa_last_launches()).count("1")
+            marks[l][1].record(stream)
+            a2 = attn.reshape(tokens, -1)
+            if decode:
+                out = (torch.matmul(a2, w_o[l], out=reducer.slot((tokens, DM))) if reducer is not None
+                       else a2 @ w_o[l])
+                marks[l][2].record(stream)
+                if reducer is not None:
+                    reducer.all_reduce_(out)
+                    launches[0] += 1
+                elif world > 1:
+                    torch.distributed.all_reduce(out)
+                marks[l][3].record(stream)
+            else:
+                for c0 in range(0, tokens, SERVE_OPROJ_CHUNK):
+                    c1 = min(tokens, c0 + SERVE_OPROJ_CHUNK)
+                    torch.matmul(a2[c0:c1], w_o[l], out=proj[:c1 - c0])
+                    if world > 1:
+                        torch.distributed.all_reduce(proj[:c1 - c0])
+                marks[l][2].record(stream)        # o_proj and its all-reduce timed together
+                marks[l][3].record(stream)
+        return decode, tokens
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def one_step(record):
+        batch = sim.schedule()
+        if not batch:
+            return None
+        marks = [[ev() for _ in range(4)] for _ in range(L)]
+        decode, tokens = run_pass(batch, marks)
+        sim.finish_pass(batch)
+        if record is not None:
+            record.append((decode, len(batch), tokens, marks))
+        return decode
+
+    clocks = ClockSampler(dev.index)
+    with clocks, QuietHost():
+        for _ in range(args.warmup):
+            one_step(None)
+        barrier()
+        torch.cuda.synchronize(dev)
+        pre0, rec0, done0, launches[0] = sim.preemptions, sim.recompute_tokens, sim.completed, 0
+        passes: list = []
+        t0, t1 = ev(), ev()
+        t0.record(stream)
+        while len(passes) < args.steps and sim.has_work:
+            one_step(passes)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        elapsed = t0.elapsed_time(t1)
+    assert pkg.read_device_error(dev) == 0, "a kernel set the device error word"
+    if reducer is not None:
+        reducer.check()
+        reducer.close()
+        barrier()
+
+    def span(kind, a, b):
+        return float(sum(m[a].elapsed_time(m[b]) for d, _, _, mk in passes if d == kind for m in mk))
+
+    sampled = sum(n for _, n, _, _ in passes)
+    stats = torch.tensor([elapsed, span(True, 0, 1), span(True, 1, 2), span(True, 2, 3), span(False, 0, 1),
+                          span(False, 1, 3)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+    elapsed, dec_attn, dec_gemm, dec_ar, pre_attn, pre_proj = stats.tolist()
+    if rank != 0:
+        return
+    n_dec = sum(1 for d, _, _, _ in passes if d)
+    n_pre = len(passes) - n_dec
+    dec_tokens = sum(n for d, n, _, _ in passes if d)
+    pre_tokens = sum(t for d, _, t, _ in passes if not d)
+    line = {
+        "metric": METRIC, "value": sampled / (elapsed / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": len(passes), "warmup": args.warmup, "ms_per_step": elapsed / max(1, len(passes)),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 5 served: Llama-3-70B-shape GQA (64 q / 8 kv heads, head_dim 128, "
+                               f"bf16, {L} layers, d_model {DM}), {NREQ} requests with contexts lognormal mean 8192 "
+                               "clipped 128..32768 (outputs lognormal median 64, clipped 1..512), KV heads sharded "
+                               f"over {world} GPU(s), row-split o_proj + one all-reduce per layer; the reference "
+                               "scheduler's policy (prefill-priority passes, recompute preemption) over a pool of "
+                               f"~90 % of free HBM",
+                   "model": "llama3-70b-shape attention + o_proj (random-init)", "requests": NREQ, "layers": L,
+                   "kv_heads_per_gpu": Hkv, "q_heads_per_gpu": Hq,
+                   "pool_blocks": nb, "pool_gb": round(pool_bytes / 1e9, 1),
+                   "pool_frac_of_hbm": round(pool_bytes / total_b, 3),
+                   "resident_at_start": resident, "running_at_end": len(sim.running),
+                   "waiting_at_end": len(sim.waiting) + len(sim.preempted),
+                   "l2": "every layer's pool is its own allocation (GBs, >> 126 MB L2)",
+                   "parallelism": f"tp{world} (KV-head sharding)" if world > 1 else "tp1"},
+        "passes": {"decode": n_dec, "prefill": n_pre, "decode_tokens_sampled": dec_tokens,
+                   "prefill_tokens_fed": pre_tokens, "preemptions": sim.preemptions - pre0,
+                   "recompute_tokens": sim.recompute_tokens - rec0, "completed": sim.completed - done0},
+        "time_split_ms": {"decode_attention": dec_attn, "decode_o_proj": dec_gemm, "decode_all_reduce": dec_ar,
+                          "prefill_attention": pre_attn, "prefill_o_proj_and_all_reduce": pre_proj,
+                          "total": elapsed},
+        "all_reduce_share_of_decode_passes": (dec_ar / (dec_attn + dec_gemm + dec_ar)) if n_dec else None,
+        "cpu_baseline": None,
+        "e2e": None,
+        "gpu_launches": launches[0],
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+class SimSeq:
+    """One request in ``ServeSim``: token counts only (no token ids are needed to drive
+    the attention path)."""
+
+    __slots__ = ("sid", "prompt_len", "max_tokens", "generated", "num_cached", "blocks", "state", "preempted_step",
+                 "preemptions")
+
+    def __init__(self, sid: int, prompt_len: int, max_tokens: int):
+        self.sid, self.prompt_len, self.max_tokens = sid, prompt_len, max_tokens
+        self.generated, self.num_cached, self.blocks = 0, 0, []
+        self.state, self.preempted_step, self.preemptions = "waiting", -1, 0
+
+    @property
+    def total_len(self) -> int:
+        return self.prompt_len + self.generated
+
+    @property
+    def feed(self) -> int:
+        """Tokens of the next pass: the whole history when nothing is cached (prefill or
+        a recompute), else the one token sampled last."""
+        return self.total_len - self.num_cached
+
+    @property
+    def prefilling(self) -> bool:
+        return self.num_cached == 0 or self.feed > 1
+
+    @property
+    def after_next(self) -> int:
+        return self.num_cached + self.feed
+
+
+class ServeSim:
+    """The reference scheduler's policy (inference_server/core/scheduler.py:184-437) over
+    token counts, for config 5's pool-bound serving run.  Restated, not imported, so the
+    bench runs where the reference is not installed; ``tests/test_bench_workload.py``
+    checks it step for step against the reference ``Scheduler`` with a fake executor.
+
+    Per step: evict finished sequences (their blocks freed); admit preempted sequences
+    first, then waiting ones, FIFO with head-of-line blocking, while a slot is free and
+    the sequence's next-pass blocks fit in the free list less the running set's own
+    next-pass growth, never on the step it was preempted; select the prefilling
+    sequences if any, else every running one; grow each selected sequence's blocks in
+    batch order, preempting the most recently admitted running sequence on exhaustion
+    (recompute: its blocks freed, nothing cached, back to the front of the preempted
+    queue).  The caller runs the pass and then calls ``finish_pass``.  Blocks come from
+    a LIFO free list like the reference allocator's."""
+
+    def __init__(self, num_blocks: int, block_size: int, max_running: int):
+        self.num_blocks, self.bs, self.max_running = num_blocks, block_size, max_running
+        self.free = list(reversed(range(num_blocks)))
+        self.waiting: list[SimSeq] = []
+        self.preempted: list[SimSeq] = []
+        self.running: list[SimSeq] = []
+        self.step_count = 0
+        self.preemptions = 0
+        self.recompute_tokens = 0       # tokens re-prefilled after a preemption
+        self.completed = 0
+
+    def blocks_for(self, n: int) -> int:
+        return -(-n // self.bs)
+
+    def add(self, seq: SimSeq) -> None:
+        if self.blocks_for(seq.prompt_len + seq.max_tokens - 1) > self.num_blocks:
+            raise ValueError(f"request {seq.sid} cannot fit the pool even alone")
+        self.waiting.append(seq)
+
+    def admit_resident(self, seq: SimSeq) -> bool:
+        """Steady-state start: admit `seq` as if its prompt had been prefilled and its
+        first token sampled (its KV is resident), if it fits by the admission rule."""
+        seq.num_cached, seq.generated = seq.prompt_len, 1
+        if len(self.running) >= self.max_running or not self._fits(seq):
+            seq.num_cached, seq.generated = 0, 0
+            return False
+        self._grow_to(seq, seq.num_cached)
+        seq.state = "running"
+        self.running.append(seq)
+        return True
+
+    @property
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.preempted or self.running)
+
+    # ---------------------------------------------------------------- the policy
+    def _needed(self, s: SimSeq) -> int:
+        return self.blocks_for(s.after_next) - len(s.blocks)
+
+    def _fits(self, s: SimSeq) -> bool:
+        reserved = sum(self._needed(r) for r in self.running)
+        return self._needed(s) <= len(self.free) - reserved
+
+    def _grow_to(self, s: SimSeq, tokens: int) -> bool:
+        need = self.blocks_for(tokens) - len(s.blocks)
+        if need <= 0:
+            return True
+        if need > len(self.free):
+            return False
+        s.blocks += [self.free.pop() for _ in range(need)]
+        return True
+
+    def _release(self, s: SimSeq) -> None:
+        self.free += s.blocks
+        s.blocks = []
+
+    def _preempt(self, v: SimSeq) -> None:
+        self._release(v)
+        self.running.remove(v)
+        v.num_cached, v.state, v.preempted_step = 0, "preempted", self.step_count
+        v.preemptions += 1
+        self.preempted.insert(0, v)
+        self.preemptions += 1
+
+    def schedule(self) -> list[SimSeq]:
+        """Steps 1-3 of a scheduler step; returns the batch to execute (maybe empty)."""
+        self.step_count += 1
+        done = [s for s in self.running if s.state == "finished"]
+        for s in done:
+            self._release(s)
+        self.running = [s for s in self.running if s.state != "finished"]
+        while len(self.running) < self.max_running:
+            queue = self.preempted if self.preempted else self.waiting
+            if not queue:
+                break
+            s = queue[0]
+            if s.preempted_step == self.step_count or not self._fits(s):
+                break
+            queue.pop(0)
+            s.state = "running"
+            self.running.append(s)
+        pre = [s for s in self.running if s.prefilling]
+        batch = pre if pre else list(self.running)
+        pending = list(batch)
+        while pending:
+            s = pending[0]
+            if self._grow_to(s, s.after_next):
+                pending.pop(0)
+                continue
+            victim = self.running[-1]
+            self._preempt(victim)
+            if victim in pending:
+                pending.remove(victim)
+            if victim in batch:
+                batch.remove(victim)
+        return batch
+
+    def finish_pass(self, batch: list[SimSeq]) -> None:
+        """Step 5: the pass cached every fed token and sampled one per sequence."""
+        for s in batch:
+            if s.num_cached == 0 and s.preemptions:
+                self.recompute_tokens += s.feed
+            s.num_cached = s.after_next
+            s.generated += 1
+            if s.generated >= s.max_tokens:
+                s.state = "finished"
+                self.completed += 1
+
+
 class PrefixWorkload:
     """BASELINE config 4 as a seeded continuous batch: `batch` running requests, each a
     shared 128-token system prefix (the same 8 physical blocks in every block table, as
@@ -801,7 +1179,7 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
     pre = _Pass(L, t_pre, Hq, Hkv, D, torch.bfloat16, dev, g)
     bt = torch.from_numpy(wl.tables).to(dev)
     sm = pkg.metadata.sm_count(dev)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
+    tile = _prefill_tile(pkg, args, Hq, Hkv, D)
     dummy = torch.zeros(1, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -1435,7 +1813,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     L, B, Hq, Hkv, D, BS = wl.layers, wl.batch, wl.heads, wl.kv_heads, wl.head_dim, wl.block_size
     f32 = WORKLOADS[args.workload]["dtype"] == "f32"
     dtype, elem = (torch.float32, 4) if f32 else (torch.bfloat16, 2)
-    tile = pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
+    tile = _prefill_tile(pkg, args, Hq, Hkv, D)
     sm = pkg.metadata.sm_count(dev)
 
     # ---- device-resident inputs
@@ -1466,6 +1844,8 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     metas_d = [plan_decode(s) for s in range(steps_total)]
     metas_p = [plan_prefill(s) for s in range(steps_total)] if wl.n_churn else [None] * steps_total
     dummy_lens = torch.zeros(1, dtype=torch.int64, device=dev)
+    _reserve_for_timing(pkg, dev, [m for m in metas_d + metas_p if m is not None], Hq, D, dtype,
+                        max(B, t_pre_max))
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
     launches = [0]
@@ -1695,6 +2075,26 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _prefill_tile(pkg, args, Hq: int, Hkv: int, D: int) -> int:
+    """Query tokens per prefill tile: the library's choice, or ``--prefill-tile-rows``
+    (256 selects the CTA-pair kernel, 128 the single-CTA kernel) divided by the group."""
+    if args.prefill_tile_rows:
+        return args.prefill_tile_rows // (Hq // Hkv)
+    return pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
+
+
+def _reserve_for_timing(pkg, dev, metas, heads: int, head_dim: int, dtype, max_tokens: int) -> None:
+    """Size the library's workspace for the largest plan and leave a cached block for the
+    largest attention output before any timed region, so no allocation (a cudaMalloc,
+    or the caching allocator freeing and retrying when HBM is nearly full) happens while
+    launches are being timed."""
+    lib = pkg._lib.lib()
+    ws = max(int(lib.pa_workspace_bytes(pkg._lib.ctypes.byref(m.plan), heads, head_dim)) for m in metas)
+    pkg.attention._workspace(dev, ws)
+    tmp = torch.empty(max_tokens * heads * head_dim, dtype=dtype, device=dev)
+    del tmp
+
+
 def _traffic_per_call(ctx_tokens: float):
     """DRAM bytes per decode launch from the committed ncu summary, scaled from the
     captured case to this workload by context tokens (traffic grows with the K/V bytes
@@ -1730,6 +2130,9 @@ def main() -> None:
     ap.add_argument("--cpu-sample-prompts", type=int, default=2, help="churn prompts in the CPU baseline's sample")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tile-rows", type=int, default=0,
+                    help="(token, head) rows per prefill tile: 256 = CTA-pair kernel, 128 = single-CTA kernel "
+                         "(default: the library's choice)")
     ap.add_argument("--graphs", action="store_true",
                     help="config4: run the decode pass as a captured CUDA graph per step")
     ap.add_argument("--tp", type=int, default=2, help="oproj: the tensor-parallel size whose per-rank k is run")
@@ -1778,6 +2181,8 @@ def main() -> None:
         elif args.workload == "blocks":
             run_blocks(args, rank, world, local_rank)
         elif args.workload == "config5":
+            run_serve_tp(args, rank, world, local_rank)
+        elif args.workload == "config5-decode":
             run_tp(args, rank, world, local_rank)
         elif args.workload == "oproj":
             run_oproj(args, rank, world, local_rank)

@@ -74,3 +74,75 @@ def test_config3_workload_is_the_recorded_one():
     assert wl.n_churn == 13
     assert 128 <= wl.ctx0.min() and wl.ctx0.max() <= 16384
     assert 256 <= wl.prompts.min() and wl.prompts.max() <= 2048
+
+
+# ------------------------------------------------------------------ ServeSim vs the reference
+def _sim_log(requests, num_blocks, max_running, steps):
+    sim = bench.ServeSim(num_blocks, 16, max_running)
+    seqs = [bench.SimSeq(i, p, m) for i, (p, m) in enumerate(requests)]
+    for s in seqs:
+        sim.add(s)
+    log = []
+    for _ in range(steps):
+        if not sim.has_work:
+            break
+        batch = sim.schedule()
+        if batch:
+            log.append([(f"r{s.sid}", s.feed) for s in batch])
+            sim.finish_pass(batch)
+    return log, sim.preemptions, sim.completed
+
+
+def _reference_log(requests, num_blocks, max_running, steps, monkeypatch):
+    import _reference
+
+    _reference.require()
+    sys.path.insert(0, str(_reference.REF))
+    import importlib
+
+    config = importlib.import_module("inference_server.config")
+    scheduler = importlib.import_module("inference_server.core.scheduler")
+    allocator = importlib.import_module("inference_server.core.block_allocator")
+    sequence = importlib.import_module("inference_server.core.sequence")
+    monkeypatch.setattr(config.CONFIG, "block_size", 16)
+    monkeypatch.setattr(config.CONFIG, "max_running", max_running)
+    monkeypatch.setattr(config.CONFIG, "preemption", "recompute")
+    monkeypatch.setattr(config.CONFIG, "max_queue_depth", 10_000)
+
+    class Counting:
+        def __init__(self):
+            self.log = []
+
+        def execute(self, seqs):
+            self.log.append([(s.seq_id, len(s.next_input_ids)) for s in seqs])
+            for s in seqs:
+                s.num_cached += len(s.next_input_ids)
+            return [1] * len(seqs)
+
+    ex = Counting()
+    sched = scheduler.Scheduler(ex, -1, allocator=allocator.BlockAllocator(num_blocks), pool=None)
+    for i, (p, m) in enumerate(requests):
+        sched.add(sequence.Sequence(seq_id=f"r{i}", prompt_token_ids=[7] * p, max_tokens=m))
+    for _ in range(steps):
+        if not sched.has_work:
+            break
+        sched.step()
+    st = sched.stats()
+    return ex.log, st["preemptions"], st["completed"]
+
+
+@pytest.mark.parametrize("num_blocks,max_running,seed", [(40, 8, 0), (64, 16, 1), (2000, 32, 2)])
+def test_serve_sim_takes_the_reference_schedulers_decisions(num_blocks, max_running, seed, monkeypatch):
+    """config 5's serving run uses ServeSim in place of the reference Scheduler; on the
+    same requests both run the same passes in the same order (sequences, tokens fed),
+    preempt as often and complete as many requests — including pools small enough that
+    recompute preemption fires repeatedly."""
+    rng = np.random.default_rng(seed)
+    reqs = [(int(rng.integers(20, 300)), int(rng.integers(5, 90))) for _ in range(24)]
+    reqs = [(p, m) for p, m in reqs if -(-(p + m - 1) // 16) <= num_blocks]
+    sim = _sim_log(reqs, num_blocks, max_running, 5000)
+    ref = _reference_log(reqs, num_blocks, max_running, 5000, monkeypatch)
+    assert sim[0] == ref[0]
+    assert sim[1:] == ref[1:]
+    if num_blocks <= 64:
+        assert sim[1] > 0
