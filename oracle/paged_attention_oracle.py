@@ -14,6 +14,9 @@ integer arithmetic around it.  Every function cites the reference file:line it f
   paged_attention_gather inference_server/core/attention.py:92-127    (dispatch decode/ragged)
   _decode_batched        inference_server/core/attention.py:130-153
   _ragged_loop           inference_server/core/attention.py:156-187
+  paged_attention_mirror inference_server/core/attention_triton.py:309-384
+                         (paged_attention_reference: the Triton kernel's per-(token,
+                         head) block loop and online softmax, the secondary oracle)
   token_map              inference_server/core/attention_triton.py:129-150 (_token_map)
   slots                  inference_server/core/block_table.py:143-159 (BlockTable.slots)
   pack_step              inference_server/core/paged_executor.py:211-263 (_pack)
@@ -192,6 +195,56 @@ def _ragged_loop(query, k_pool, v_pool, block_tables, context_lens, query_lens, 
         probs = round_to(_softmax_f32(scores), dtype)
         out[start:start + q_len] = round_to(np.matmul(probs, v), dtype).transpose(1, 0, 2)
         start += q_len
+    return out
+
+
+def paged_attention_mirror(query, k_pool, v_pool, block_tables, context_lens, query_lens,
+                           scale: float, dtype: str = "f32") -> np.ndarray:
+    """The online-softmax order of the reference's Triton kernel, as its PyTorch mirror
+    states it (attention_triton.py:309-384): for every (token, head), q is scaled in
+    float32 before the dot products; the keys ``0 .. q_pos`` are walked one pool block at
+    a time (block ``b`` of the sequence's row, keys past ``q_pos`` masked to -inf);
+    per block ``m_new = max(m, max s)``, ``alpha = exp(m - m_new)``, ``p = exp(s - m_new)``,
+    ``l = alpha*l + sum p``, ``acc = alpha*acc + p.v``; the output is ``acc / l`` rounded
+    once to the storage dtype.  Everything runs in float32 (the mirror's ``.float()``);
+    heads are vectorised here, the mirror loops over them."""
+    query = np.asarray(query, dtype=np.float32)
+    k_pool = np.asarray(k_pool, dtype=np.float32)
+    v_pool = np.asarray(v_pool, dtype=np.float32)
+    block_tables = np.asarray(block_tables, dtype=np.int64)
+    check(query.shape, k_pool.shape, block_tables, context_lens, query_lens)
+    num_tokens, num_heads, head_dim = query.shape
+    block_size, num_kv_heads = k_pool.shape[1], k_pool.shape[2]
+    group = num_heads // num_kv_heads
+    out = np.empty_like(query)
+    if num_tokens == 0:
+        return out
+    seq_idx, q_pos, _ = token_map(context_lens, query_lens)
+    kv_of_head = np.arange(num_heads) // group
+    offs = np.arange(block_size)
+    for tok in range(num_tokens):
+        seq, pos = int(seq_idx[tok]), int(q_pos[tok])
+        n_keys = pos + 1
+        q = query[tok] * np.float32(scale)                              # [H, D]
+        m = np.full(num_heads, -np.inf, dtype=np.float32)
+        l = np.zeros(num_heads, dtype=np.float32)
+        acc = np.zeros((num_heads, head_dim), dtype=np.float32)
+        for blk in range(-(-n_keys // block_size)):
+            phys = int(block_tables[seq, blk])
+            valid = blk * block_size + offs < n_keys                    # [BS]
+            k = k_pool[phys][:, kv_of_head, :]                          # [BS, H, D]
+            v = v_pool[phys][:, kv_of_head, :]
+            k = np.where(valid[:, None, None], k, np.float32(0))
+            v = np.where(valid[:, None, None], v, np.float32(0))
+            s = np.einsum("bhd,hd->hb", k, q, dtype=np.float32)          # [H, BS]
+            s = np.where(valid[None, :], s, np.float32(-np.inf))
+            m_new = np.maximum(m, s.max(axis=1))
+            alpha = np.exp(m - m_new, dtype=np.float32)
+            p = np.exp(s - m_new[:, None], dtype=np.float32)
+            l = alpha * l + p.sum(axis=1, dtype=np.float32)
+            acc = alpha[:, None] * acc + np.einsum("hb,bhd->hd", p, v, dtype=np.float32)
+            m = m_new
+        out[tok] = round_to(acc / l[:, None], dtype)
     return out
 
 

@@ -11,6 +11,9 @@ What it records, all from the reference's own code on CPU:
   uses (tests/test_paged_attention.py, tests/test_paged_attention_triton.py:74-84,
   :118-128, :172-192) plus the serving shapes this project targets (GPT-2 12/12/64 and
   Llama-3 32/8/128, 16/2/128 at block size 16) in fp32, fp16 and bf16.
+* ``mirror.npz``: the output of ``paged_attention_reference`` (attention_triton.py:309-384,
+  the PyTorch mirror of the Triton kernel's online softmax) on the inputs of a subset of
+  the ``attn_<case>`` files (key: the case name).
 * ``token_map.npz``: ``_token_map`` (attention_triton.py:129-150), including the
   known-answer case of tests/test_paged_attention_triton.py:140-147.
 * ``pack.npz``: ``PagedExecutor._pack`` (paged_executor.py:211-263) over real
@@ -87,6 +90,11 @@ _case("llama8b_decode_f16", [(40, 1), (16, 1), (70, 1)], bs=16, d=128,
 TORCH_DTYPE = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
 
+# Cases whose inputs also go through the reference's online-softmax mirror.
+MIRROR_CASES = ["prefill_ragged", "decode_ragged", "mixed", "partial_query", "padding_hits_block0_s1", "gqa_kv1",
+                "non_pow2_bs6_d12", "mixed_bf16", "prod_long_bs16_d64", "llama70b_group8_bf16"]
+
+
 def build(lengths, bs, d, heads, kv_heads, num_blocks, dtype, seed):
     """Seeded inputs in the layout of the reference tests' `_build`."""
     g = torch.Generator().manual_seed(seed)
@@ -117,9 +125,10 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the llm-inference-server checkout")
     ap.add_argument("--only", nargs="*", default=None,
-                    help="regenerate only these outputs: attn token_map pack kv_append blocks gpt2_greedy")
+                    help="regenerate only these outputs: attn mirror token_map pack kv_append blocks gpt2_greedy")
     args = ap.parse_args()
-    want = set(args.only) if args.only else {"attn", "token_map", "pack", "kv_append", "blocks", "gpt2_greedy"}
+    want = set(args.only) if args.only else {"attn", "mirror", "token_map", "pack", "kv_append", "blocks",
+                                             "gpt2_greedy"}
     os.environ.setdefault("DEVICE", "cpu")
     sys.path.insert(0, str(Path(args.reference).resolve()))
 
@@ -142,6 +151,16 @@ def main() -> None:
             out=_store(out, dt), block_tables=bt.numpy(), context_lens=cl.numpy(),
             query_lens=ql.numpy(), scale=np.float64(scale), dtype=np.bytes_(dt),
         )
+
+    if "mirror" in want:
+        from inference_server.core.attention_triton import paged_attention_reference
+
+        mirror = {}
+        for name in MIRROR_CASES:
+            lengths, kw = CASES[name]
+            q, kp, vp, bt, cl, ql = build(lengths, **kw)
+            mirror[name] = _store(paged_attention_reference(q, kp, vp, bt, cl, ql, kw["d"] ** -0.5), kw["dtype"])
+        np.savez_compressed(HERE / "mirror.npz", **mirror)
 
     if "gpt2_greedy" in want:
         _gpt2_greedy(PagedExecutor, PagedKVPool, ModelDims, BlockAllocator, BlockTable, Sequence)

@@ -11,7 +11,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from _golden import attention_cases, load, load_attention
+from _golden import attention_cases, decode_stored, load, load_attention
 
 CASES = attention_cases()
 
@@ -35,6 +35,37 @@ def test_oracle_matches_reference_gather(case, oracle):
         # accumulation order inside the two matmuls, then one half-precision rounding.
         ulp = 2.0 ** -7 if g["dtype"] == "bf16" else 2.0 ** -10
         np.testing.assert_allclose(out, g["out"], atol=2 * ulp, rtol=2 * ulp)
+
+
+MIRROR_CASES = sorted(load("mirror").keys())
+
+
+@pytest.mark.parametrize("case", MIRROR_CASES)
+def test_mirror_matches_reference_mirror(case, oracle):
+    """The secondary oracle: the reference's PyTorch mirror of its Triton kernel
+    (attention_triton.py:309-384: per-block online softmax, float32 throughout) against
+    this oracle's restatement, on the same inputs."""
+    g = load_attention(case)
+    want = decode_stored(load("mirror")[case], g["dtype"])
+    out = oracle.paged_attention_mirror(g["query"], g["k_pool"], g["v_pool"], g["block_tables"],
+                                        g["context_lens"], g["query_lens"], g["scale"], g["dtype"])
+    if g["dtype"] == "f32":
+        np.testing.assert_allclose(out, want, atol=2e-6, rtol=2e-6)
+    else:  # float32 summation order, then one rounding to the storage dtype
+        ulp = 2.0 ** -7 if g["dtype"] == "bf16" else 2.0 ** -10
+        np.testing.assert_allclose(out, want, atol=ulp, rtol=ulp)
+
+
+@pytest.mark.parametrize("case", MIRROR_CASES)
+def test_mirror_agrees_with_gather(case, oracle):
+    """The two reference algorithms (gather path and the kernel mirror) agree within the
+    reference's own tolerance for its mirror tier (tests/test_paged_attention_triton.py:97-128:
+    1e-5 in fp32; the half cases within the 2e-2 kernel-tier bound)."""
+    g = load_attention(case)
+    out = oracle.paged_attention_mirror(g["query"], g["k_pool"], g["v_pool"], g["block_tables"],
+                                        g["context_lens"], g["query_lens"], g["scale"], g["dtype"])
+    tol = 1e-5 if g["dtype"] == "f32" else 2e-2
+    np.testing.assert_allclose(out, g["out"], atol=tol, rtol=tol)
 
 
 def test_token_map_known_answer(oracle):
