@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from _batches import compact_subbatch, lognormal_contexts, ragged_batch, ragged_batch_device, subset_rows
-from _golden import TOL, attention_cases, load_attention
+from _golden import TOL, attention_cases, load, load_attention
 
 pytestmark = pytest.mark.gpu
 
@@ -51,6 +51,24 @@ def test_matches_reference_golden(pkg, case):
                torch.from_numpy(g["query_lens"]), g["scale"])
     assert out.dtype == td and tuple(out.shape) == g["out"].shape
     _close(out.float().cpu().numpy(), g["out"], g["dtype"], case)
+    assert pkg.read_device_error() == 0
+
+
+@pytest.mark.parametrize("case", sorted(load("mirror").keys()))
+def test_mirror_cuda_matches_online_softmax_mirror(pkg, oracle, case):
+    """The secondary oracle: the CUDA kernels against the reference's online-softmax
+    order (its Triton kernel's PyTorch mirror, attention_triton.py:309-384, restated in
+    the oracle and pinned to the mirror's own outputs) on the mirror's cases."""
+    g = load_attention(case)
+    td = DT[g["dtype"]]
+    q = torch.from_numpy(g["query"]).to(td)
+    kp = torch.from_numpy(g["k_pool"]).to(td)
+    vp = torch.from_numpy(g["v_pool"]).to(td)
+    out = _run(pkg, q, kp, vp, torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]),
+               torch.from_numpy(g["query_lens"]), g["scale"])
+    ref = oracle.paged_attention_mirror(g["query"], g["k_pool"], g["v_pool"], g["block_tables"], g["context_lens"],
+                                        g["query_lens"], g["scale"], g["dtype"])
+    _close(out.float().cpu().numpy(), ref, g["dtype"], case)
     assert pkg.read_device_error() == 0
 
 
