@@ -380,6 +380,45 @@ def _torch_gather_reference(q, kp, vp, bt, cl, ql, scale, rows=512):
     return out
 
 
+@pytest.mark.parametrize("workload", ["config2-f32", "config2-bf16", "config3-decode", "config3-churn"])
+def test_full_size_batches_every_sequence(pkg, oracle, workload):
+    """BASELINE configs 2 and 3 at full size with EVERY sequence checked (the sampled
+    tests above re-compute a few with the numpy oracle): config 2's 256 decode rows
+    (GPT-2 heads, fp32 and bf16), config 3's 256 decode rows (32/8/128 bf16, contexts
+    mean 4096 up to 16384) and a full step of 13 churn prompts (256..2048 tokens) through
+    the tcgen05 prefill, against the gather path's arithmetic run in torch on the GPU
+    (pinned to the oracle on two of the sequences here)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    if workload.startswith("config2"):
+        dt = workload.split("-")[1]
+        ctx = lognormal_contexts(256, 1024, 0.9, 16, 8192, seed=0)
+        lengths = [(int(c), 1) for c in ctx]
+        heads, kv_heads, d, td = 12, 12, 64, DT[dt]
+    elif workload == "config3-decode":
+        dt = "bf16"
+        ctx = lognormal_contexts(256, 4096 * np.exp(-0.405), 0.9, 128, 16384, seed=0)
+        lengths = [(int(c), 1) for c in ctx]
+        heads, kv_heads, d, td = 32, 8, 128, torch.bfloat16
+    else:
+        dt = "bf16"
+        rng = np.random.default_rng(0)
+        lengths = [(int(n), int(n)) for n in rng.integers(256, 2049, size=13)]
+        heads, kv_heads, d, td = 32, 8, 128, torch.bfloat16
+    batch = ragged_batch_device(lengths, bs=16, d=d, heads=heads, kv_heads=kv_heads, dtype=td, device=DEV)
+    q, kp, vp, bt, cl, ql = batch
+    out = pkg.paged_attention_cuda(q, kp, vp, bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
+    if workload == "config3-churn":
+        assert pkg._lib.last_launches() == {"prefill_tc"}
+    ref = _torch_gather_reference(q, kp, vp, bt, cl, ql, d ** -0.5).cpu().numpy()
+    _close(out.float().cpu().numpy(), ref, dt, workload)
+    # the torch restatement itself, pinned to the oracle on the shortest and longest rows
+    picks = [int(np.argmin([c for c, _ in lengths])), int(np.argmax([c for c, _ in lengths]))]
+    sub = compact_subbatch(*batch, lengths, picks, 16)
+    want = oracle.paged_attention_gather(*sub, d ** -0.5, dt)
+    _close(ref[subset_rows(lengths, picks)], want, dt, "torch restatement vs oracle")
+    assert pkg.read_device_error() == 0
+
+
 def test_long_context_prefill_matches_reference(pkg, oracle):
     """Long rows of the tcgen05 prefill at the Llama-8B shape: a 4,600-token prompt and a
     prefix-cache hit of 700 new tokens over a 9,300-token context (plus a decode row),
