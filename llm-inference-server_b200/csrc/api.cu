@@ -540,10 +540,12 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
     if (r != CUDA_SUCCESS) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
     return PA_OK;
   };
-  CUtensorMap ta, tw;
+  CUtensorMap ta, tw, tw_half;
   int32_t st = kmajor(a, rows, a_row_stride, kOprojTile, &ta);
   if (st != PA_OK) return st;
   st = kmajor(w, n, k, kOprojTileN, &tw);
+  if (st != PA_OK) return st;
+  st = kmajor(w, n, k, kOprojTileN / 2, &tw_half);
   if (st != PA_OK) return st;
   p.stage_offset = stage_offset;
   p.out_offset = out_offset;
@@ -560,7 +562,7 @@ int32_t pa_oproj_allreduce(const void* a, int64_t a_row_stride, int32_t rows, in
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t vecs = int64_t(rows) * (n / world) * 2 / 16;  // 16-byte vectors of this rank's slice
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(sms, (vecs + kPeerThreads - 1) / kPeerThreads)));
-  cudaError_t e = launch_oproj_allreduce(dtype, ta, tw, p, grid, static_cast<cudaStream_t>(stream_ptr));
+  cudaError_t e = launch_oproj_allreduce(dtype, ta, tw, tw_half, p, grid, static_cast<cudaStream_t>(stream_ptr));
   if (e != cudaSuccess) return cuda_fail(e, "oproj_allreduce launch");
   return PA_OK;
 }

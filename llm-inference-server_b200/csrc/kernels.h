@@ -174,8 +174,9 @@ cudaError_t launch_prefill_pair(int dtype, int group, const CUtensorMap& tk, con
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);
-// ta: a as (k, rows), box (64, 128); tw: w as (k, n), box (64, 256); 128-byte swizzle.
-cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const OprojParams& p,
-                                   int gather_grid, cudaStream_t stream);
+// ta: a as (k, rows), box (64, 128); tw: w as (k, n), box (64, 256); tw_half: the same map
+// with box (64, 128) (the CTA-pair GEMM, used when rows > 128); 128-byte swizzle.
+cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tw_half,
+                                   const OprojParams& p, int gather_grid, cudaStream_t stream);
 
 }  // namespace pa

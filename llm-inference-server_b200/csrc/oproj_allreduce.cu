@@ -15,6 +15,13 @@
 //     epilogue.  128 x 256 moves a quarter fewer bytes per flop than 128 x 128 tiles,
 //     which were measured slower in this kernel.  The last CTA to finish releases this
 //     rank's "ready" flag into every rank's flag area.
+//   oproj_push_pair_kernel  the same GEMM on CTA pairs (rows > 128): a cluster of two CTAs
+//     computes one 256 x 256 tile with M = 256 tcgen05 MMAs (cta_group::2).  Each CTA loads
+//     its own 128 rows of a and 128 of the tile's 256 rows of w (K-major) into its 6-stage
+//     ring, so an SM moves a third fewer operand bytes per flop than with 128 x 256 tiles
+//     (whose TMA delivery the profile shows the single-CTA GEMM waiting on); the leader's
+//     MMA warp issues for both and commits to both CTAs' barriers, and each CTA's epilogue
+//     pushes its own 128 x 256 accumulator exactly as above.  No load uses multicast.
 //   oproj_gather_kernel the owner waits for every rank's ready flag, sums its slice over
 //     the `world` staged partials in rank order in float32 (so every rank receives the
 //     same bytes), rounds once and stores the sum into every rank's output slot: the
@@ -30,6 +37,7 @@
 // multi-GPU path; this replaces the row-split o_proj GEMM plus torch.distributed.all_reduce.
 #include "peer_common.cuh"
 #include "tc_common.cuh"
+#include "tc_pair.cuh"
 
 namespace pa {
 
@@ -200,6 +208,165 @@ __global__ void __launch_bounds__(kOpThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM
+constexpr int kOp2Stages = 6;
+constexpr int kOp2Box = 128 * 128;                 // 128 rows x 64 k (16-bit), a or w
+constexpr int kOp2Stage = 2 * kOp2Box;             // this CTA's a box, then its w box
+constexpr int kOp2BarOff = kOp2Stages * kOp2Stage;
+constexpr int kOp2Smem = kOp2BarOff + 128;
+static_assert(kOprojTile * kOpPitch <= kOp2BarOff, "the output tile reuses the ring");
+static_assert(kOp2Smem <= 227 * 1024, "shared memory per CTA");
+
+struct OpBars2 {
+  uint64_t full[kOp2Stages], empty[kOp2Stages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  uint32_t last;
+};
+static_assert(sizeof(OpBars2) <= 128, "barrier area");
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kOpThreads, 1)
+    oproj_push_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
+                           const __grid_constant__ OprojParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  OpBars2* bars = reinterpret_cast<OpBars2*>(smem + kOp2BarOff);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int n0 = (blockIdx.x >> 1) * kOprojTileN;                   // the pair's 256 output columns
+  const int m0 = blockIdx.y * 2 * kOprojTile + int(rank) * kOprojTile;  // this CTA's 128 rows
+  const int wrow0 = n0 + int(rank) * (kOprojTileN / 2);             // this CTA's half of w's rows
+  const int ksteps = p.k / kOprojKStep;
+
+  if (warp == 5) {
+    tmem_alloc_pair(&bars->tmem_base, kOprojTileN);
+    tmem_relinquish_pair();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kOp2Stages; ++s) {
+      mbar_init(&bars->full[s], 2);     // both CTAs' expect-tx arrivals (leader's copy is used)
+      mbar_init(&bars->empty[s], 1);    // the leader's MMA commit, multicast to both CTAs
+    }
+    mbar_init(&bars->acc_full, 1);
+    fence_mbar_init();
+  }
+  // Both CTAs' barriers and TMEM exist before any cross-CTA arrival, load or MMA.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tacc = bars->tmem_base;
+  auto leader_bar = [&](uint64_t* b) { return mapa_rank(smem_u32(b), 0); };
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tw);
+      bool ok = true;
+      for (int j = 0; j < ksteps; ++j) {
+        const int s = j % kOp2Stages;
+        if (j >= kOp2Stages && !mbar_wait(&bars->empty[s], ((j / kOp2Stages) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * kOp2Stage;
+        if (leader)
+          mbar_arrive_expect_tx(&bars->full[s], kOp2Stage);
+        else
+          mbar_arrive_expect_tx_remote(leader_bar(&bars->full[s]), kOp2Stage);
+        tma_load_2d_pair(st, &ta, j * kOprojKStep, m0, leader_bar(&bars->full[s]));
+        tma_load_2d_pair(st + kOp2Box, &tw, j * kOprojKStep, wrow0, leader_bar(&bars->full[s]));
+      }
+      if (!ok) set_error(p.err, kErrWaitTimeout);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16<T>(2 * kOprojTile, kOprojTileN, false);
+      bool ok = true;
+      for (int j = 0; j < ksteps; ++j) {
+        const int s = j % kOp2Stages;
+        if (!mbar_wait(&bars->full[s], (j / kOp2Stages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * kOp2Stage), w0 = a0 + kOp2Box;
+#pragma unroll
+        for (int kk = 0; kk < kOprojKStep / 16; ++kk)
+          umma_pair_ss(tacc, smem_desc_sw128(a0 + kk * 32, 16, 1024), smem_desc_sw128(w0 + kk * 32, 16, 1024),
+                       idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_pair(&bars->empty[s]);
+      }
+      if (!ok) set_error(p.err, kErrWaitTimeout);
+      umma_commit_pair(&bars->acc_full);  // also after an error, so neither epilogue is left waiting
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 0-3)
+    // This CTA's 128 rows of the tile are its TMEM lanes; every MMA and every TMA load has
+    // completed once acc_full fires, so the ring's shared memory is free for the staged tile.
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full, 0));
+    if (got) {
+      tc_fence_after();
+      const int r = warp * 32 + lane;
+      const uint32_t lane_base = uint32_t(warp * 32) << 16;
+#pragma unroll
+      for (int c = 0; c < kOprojTileN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tacc + lane_base + 32 * c, v);
+        tmem_wait_ld();
+        uint4* dst = reinterpret_cast<uint4*>(smem + r * kOpPitch + c * 64);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_pair<T>(v[8 * q], v[8 * q + 1]), pack_pair<T>(v[8 * q + 2], v[8 * q + 3]),
+                              pack_pair<T>(v[8 * q + 4], v[8 * q + 5]), pack_pair<T>(v[8 * q + 6], v[8 * q + 7]));
+      }
+    } else if (lane == 0) {
+      set_error(p.err, kErrWaitTimeout);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    if (got) {
+      const int slice = p.n / p.world, owner = n0 / slice, col0 = n0 - owner * slice;
+      uint8_t* dst = p.base[owner] + p.stage_offset + (int64_t(p.rank) * p.rows * slice + col0) * 2;
+      const int ch = tid & 31;
+#pragma unroll 4
+      for (int row = tid >> 5; row < kOprojTile; row += 4) {
+        if (m0 + row < p.rows) {
+          const uint4 v = *reinterpret_cast<const uint4*>(smem + row * kOpPitch + ch * 16);
+          *reinterpret_cast<uint4*>(dst + int64_t(m0 + row) * slice * 2 + ch * 16) = v;
+        }
+      }
+    }
+  }
+
+  // ---- completion, as in oproj_push_kernel: the last CTA releases this rank's ready flag.
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(p.base[p.rank] + p.flags_offset);
+  if (tid == 0) {
+    __threadfence_system();
+    uint32_t* counter = my_flags + kPeerCounter;
+    const uint32_t last = atomicAdd(counter, 1u) == gridDim.x * gridDim.y - 1 ? 1u : 0u;
+    if (last) *counter = 0;  // ready for the next call (stream-ordered)
+    bars->last = last;
+  }
+  __syncthreads();
+  if (bars->last && tid < p.world) {
+    __threadfence_system();
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_flags + kPeerEpoch) + 1;
+    st_release_sys(reinterpret_cast<uint32_t*>(p.base[tid] + p.flags_offset) + kPeerReady + p.rank, epoch);
+  }
+  // Neither CTA frees TMEM or leaves while the pair's MMAs may still read its peer.
+  cluster_sync_all();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc_pair(tacc, kOprojTileN);
+  }
+}
+
 // WMAX: the world-size bucket (1, 2, 4 or 8); U = 16 / WMAX vectors per thread per round
 // (8 for a single rank), so each thread has up to 16 staged loads in flight before it
 // reduces.
@@ -271,9 +438,10 @@ __global__ void __launch_bounds__(kPeerThreads) oproj_gather_kernel(const __grid
 }
 
 template <typename T>
-static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const OprojParams& p, int gather_grid,
-                            cudaStream_t stream) {
+static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tw_half,
+                            const OprojParams& p, int gather_grid, cudaStream_t stream) {
   auto push = oproj_push_kernel<T>;
+  auto push2 = oproj_push_pair_kernel<T>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[64] = {};
@@ -282,10 +450,19 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const 
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(push, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(push2, cudaFuncAttributeMaxDynamicSharedMemorySize, kOp2Smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(push2, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(p.n / kOprojTileN, (p.rows + kOprojTile - 1) / kOprojTile);
-  push<<<grid, kOpThreads, kOpSmem, stream>>>(ta, tw, p);
+  if (p.rows > kOprojTile) {  // CTA pairs: 256 x 256 tiles
+    dim3 grid(2 * (p.n / kOprojTileN), (p.rows + 2 * kOprojTile - 1) / (2 * kOprojTile));
+    push2<<<grid, kOpThreads, kOp2Smem, stream>>>(ta, tw_half, p);
+  } else {
+    dim3 grid(p.n / kOprojTileN, (p.rows + kOprojTile - 1) / kOprojTile);
+    push<<<grid, kOpThreads, kOpSmem, stream>>>(ta, tw, p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.world <= 1)
@@ -299,10 +476,10 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const 
   return cudaGetLastError();
 }
 
-cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const OprojParams& p,
-                                   int gather_grid, cudaStream_t stream) {
-  if (dtype == PA_DTYPE_BF16) return launch_t<__nv_bfloat16>(ta, tw, p, gather_grid, stream);
-  if (dtype == PA_DTYPE_F16) return launch_t<__half>(ta, tw, p, gather_grid, stream);
+cudaError_t launch_oproj_allreduce(int dtype, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tw_half,
+                                   const OprojParams& p, int gather_grid, cudaStream_t stream) {
+  if (dtype == PA_DTYPE_BF16) return launch_t<__nv_bfloat16>(ta, tw, tw_half, p, gather_grid, stream);
+  if (dtype == PA_DTYPE_F16) return launch_t<__half>(ta, tw, tw_half, p, gather_grid, stream);
   return cudaErrorInvalidValue;
 }
 
