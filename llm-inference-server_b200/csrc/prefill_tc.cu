@@ -74,6 +74,31 @@ struct PfBars {
   uint32_t tmem_base;
 };
 
+// Packed float pairs (f32x2 arithmetic) and the three-input maximum.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {  // the hardware base-2 exponential
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -314,19 +339,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 
       const int lim = qpos - kbase;  // key column c is visible iff c <= lim
       // Four independent max / sum chains instead of one 64-long dependency chain.
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // Row maximum with three-input max (two scores per instruction, four chains).
       if (__any_sync(0xffffffffu, lim < kPfKeys - 1)) {  // the tile crosses the causal diagonal
 #pragma unroll
-        for (int c = 0; c < kPfKeys; ++c) {
-          const float v = c <= lim ? __uint_as_float(sr[c]) : -INFINITY;
-          sr[c] = __float_as_uint(v);
-          mx4[c & 3] = fmaxf(mx4[c & 3], v);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kPfKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
+        for (int c = 0; c < kPfKeys; ++c) sr[c] = c <= lim ? sr[c] : __float_as_uint(-INFINITY);
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kPfKeys; c += 2)
+        mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+      const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
       // Scores are raw q.k here; the softmax scale (> 0) is folded into the exponent.  The
       // subtracted maximum is only raised when the tile's maximum exceeds it by more than
       // kLazyRescale (log2 units): softmax is unchanged by the choice of that constant as
@@ -336,16 +358,23 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const bool grow = mx_s > m_run + kLazyRescale;
       const float m_new = grow ? mx_s : m_run;
       const float alpha = grow ? ex2(m_run - m_new) : 1.f;
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      // Exponent arguments and the row sum on packed float pairs (one f32x2 FMA / add per
+      // two scores; the same per-element rounding as scalar FMA / add).
+      const uint64_t sc2 = f2pack(p.qscale, p.qscale), mn2 = f2pack(-m_new, -m_new);
+      uint64_t rs2[2] = {0ull, 0ull};
       uint32_t pk[kPfKeys / 2];
 #pragma unroll
       for (int c = 0; c < kPfKeys; c += 2) {
-        const float e0 = ex2(fmaf(__uint_as_float(sr[c]), p.qscale, -m_new));
-        const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), p.qscale, -m_new));
-        rs4[(c >> 1) & 3] += e0 + e1;
+        float x0, x1;
+        f2unpack(fma2(f2pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, mn2), x0, x1);
+        const float e0 = ex2(x0), e1 = ex2(x1);
+        rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], f2pack(e0, e1));
         pk[c / 2] = pack2<T>(e0, e1);
       }
-      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      float r0, r1, r2, r3;
+      f2unpack(rs2[0], r0, r1);
+      f2unpack(rs2[1], r2, r3);
+      const float rs = (r0 + r1) + (r2 + r3);
       l_run = l_run * alpha + rs;
       m_run = m_new;
 
