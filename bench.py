@@ -461,20 +461,28 @@ def run_reference(args, rank: int, world: int) -> None:
             s = ReferenceStepSample(ref, wl, args.cpu_sample_seqs, args.cpu_sample_prompts, dt)
             for _ in range(args.warmup):
                 s.step_seconds()
-            times = [s.step_seconds() for _ in range(args.steps)]
+            times, wall = [], []
+            for _ in range(args.steps):
+                t0 = time.perf_counter()
+                times.append(s.step_seconds())
+                wall.append(time.perf_counter() - t0)
             value = s.tokens_per_step / float(np.mean(times))
             sample = {"value": value, "unit": "tok/s", "cores": s.cores, "kind": "reference",
-                      "sample": s.describe(len(times))}
+                      "sample": s.describe(len(times)),
+                      "extrapolated_ms_per_full_step": float(np.mean(times)) * 1e3}
+            times = wall
         else:
             one, ctx = _oracle_layer_timer(wl, args.cpu_sample_seqs, dt)
             for _ in range(args.warmup):
                 one()
-            times = [one() * wl.layers * wl.batch / args.cpu_sample_seqs for _ in range(args.steps)]
-            value = wl.batch / float(np.mean(times))
+            times = [one() for _ in range(args.steps)]
+            value = args.cpu_sample_seqs / (float(np.mean(times)) * wl.layers)
             sample = {"value": value, "unit": "tok/s", "cores": _blas_threads(), "kind": "port",
                       "sample": "reference not installed in baseline/_ref; " +
                                 _cpu_sample_text(wl, args.cpu_sample_seqs, ctx, len(times), dt)}
         ms, wl_cfg, steps = float(np.mean(times)) * 1e3, _config(args, wl, world), args.steps
+    # ms_per_step: wall time of one timed sample step on this host (the value extrapolates
+    # the sample to the whole step; see cpu_baseline.sample)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
