@@ -1474,12 +1474,15 @@ def run_engine(args, rank: int, world: int, local_rank: int) -> None:
     torch.manual_seed(0)
     model = GPT2LMHeadModel(GPT2Config()).to(dev).eval()
     pool = pkg.KVPool.from_model(model, num_blocks=2048)
-    ex = executor_mod.CudaPagedExecutor(model, None, pool)
+    ex = executor_mod.CudaPagedExecutor(model, None, pool, decode_graphs=args.graphs)
     reqs = _c1_requests(200, args.seed + rank)
     results = {}
     clocks = ClockSampler(dev.index)
     with clocks, QuietHost():
         _serve(ex, _c1_requests(8, 99), 4, 2048)          # warm-up: kernels, cuBLAS, allocator
+        if args.graphs:   # capture every (batch, width) bucket the timed runs will meet
+            for conc in sorted({4, args.batch}):
+                _serve(ex, _c1_requests(200, 99), conc, 2048)
         torch.cuda.synchronize(dev)
         for conc in sorted({4, args.batch}):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1504,6 +1507,7 @@ def run_engine(args, rank: int, world: int, local_rank: int) -> None:
                                "paged executor with ATTENTION=cuda; 2,048-block pool, block 16; 200 requests of random "
                                "token ids (prompts 16..256, outputs lognormal median 30 capped at 512); greedy",
                    "model": "gpt2-124m (random-init)", "concurrency": args.batch, "requests": 200,
+                   "decode_graphs": bool(args.graphs),
                    "passes": passes, "generated_tokens": gen,
                    "at_concurrency_4": {"tok_s": results[4][0] / (results[4][2] / 1e3), "passes": results[4][1],
                                         "ms": results[4][2]},
@@ -2142,7 +2146,8 @@ def main() -> None:
                     help="(token, head) rows per prefill tile: 256 = CTA-pair kernel, 128 = single-CTA kernel "
                          "(default: the library's choice)")
     ap.add_argument("--graphs", action="store_true",
-                    help="config4: run the decode pass as a captured CUDA graph per step")
+                    help="config4: run the decode pass as a captured CUDA graph per step; config1: the executor's "
+                         "all-decode passes as captured graphs of the whole model forward")
     ap.add_argument("--tp", type=int, default=2, help="oproj: the tensor-parallel size whose per-rank k is run")
     ap.add_argument("--allreduce", choices=["peer", "nccl", "fused"], default="peer",
                     help="config5: the o_proj all-reduce over NVLink peer memory (default), NCCL, or fused "

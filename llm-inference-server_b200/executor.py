@@ -95,10 +95,18 @@ class CudaPagedExecutor:
     """One forward pass over the pool, no policy.  Drop-in for the reference's
     ``PagedExecutor`` with ``ATTENTION=cuda``."""
 
-    def __init__(self, model, tokenizer, pool, device=None) -> None:
+    #: Batch and table-width buckets of the captured decode passes (``decode_graphs``).
+    GRAPH_BATCHES = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
+
+    def __init__(self, model, tokenizer, pool, device=None, decode_graphs: bool = False) -> None:
         self.model = model
         self.tokenizer = tokenizer
         self.pool = pool
+        #: Run all-decode passes as captured CUDA graphs of the whole model forward
+        #: (graphs.ModelDecodeGraph), one per (batch bucket, width bucket), built on
+        #: first use; other passes run eagerly.
+        self.decode_graphs = bool(decode_graphs)
+        self._graphs: dict = {}
         self.device = torch.device(device) if device is not None else pool.k[0].device
         if self.device.type != "cuda":
             raise NotImplementedError(f"ATTENTION=cuda: the paged executor needs a CUDA device, got {self.device}")
@@ -113,12 +121,53 @@ class CudaPagedExecutor:
         (paged_executor.py:172-203).  Mixed prefill/decode batches also run correctly."""
         if not seqs:
             return []
+        if self.decode_graphs and len(seqs) <= self.GRAPH_BATCHES[-1] and all(
+                len(s.next_input_ids) == 1 for s in seqs):
+            return self._execute_graph(seqs)
         input_ids, position_ids, ctx = self._pack(seqs)
         logits = self._forward(input_ids, position_ids, ctx)
         for s in seqs:
             s.num_cached += len(s.next_input_ids)
         ends = ctx.meta.cu_query_lens()[1:].long()
         return logits[0, ends - 1, :].argmax(-1).tolist()
+
+    def _execute_graph(self, seqs) -> list[int]:
+        """An all-decode pass through a captured graph: rows padded to the batch bucket
+        by repeating the last sequence, tables to a power-of-two width bucket."""
+        from .graphs import ModelDecodeGraph
+
+        bs = self.block_size
+        ctx_lens, rows, ids = [], [], []
+        for i, s in enumerate(seqs):
+            table = s.block_table
+            assert table is not None, f"{getattr(s, 'seq_id', i)} reached the paged executor without a block table"
+            after = s.num_cached + 1
+            assert table.capacity >= after, (
+                f"{getattr(s, 'seq_id', i)}: block table holds {table.capacity} slots, pass needs {after} — "
+                "the scheduler must call ensure_capacity before execute")
+            table.ensure_private((after - 1) // bs, self._copy_block)   # paged_executor.py:234-241
+            ctx_lens.append(after)
+            rows.append(table.blocks)
+            ids.append(s.next_input_ids[0])
+        b = len(seqs)
+        bp = next(x for x in self.GRAPH_BATCHES if x >= b)
+        need = max(len(r) for r in rows)
+        width = 8
+        while width < need:
+            width *= 2
+        tables = np.zeros((bp, width), dtype=np.int64)
+        for i in range(bp):
+            r = rows[min(i, b - 1)]
+            tables[i, :len(r)] = r
+        ctx = np.asarray(ctx_lens + [ctx_lens[-1]] * (bp - b), dtype=np.int64)
+        g = self._graphs.get((bp, width))
+        if g is None:
+            g = self._graphs[(bp, width)] = ModelDecodeGraph(self, bp, width)
+        g.set_step(ctx, tables, ids + [ids[-1]] * (bp - b))
+        tokens = g.run()
+        for s in seqs:
+            s.num_cached += 1
+        return tokens[:b].tolist()
 
     def reset(self) -> None:
         """Nothing survives between steps (paged_executor.py:205-208)."""

@@ -25,7 +25,7 @@ import torch
 
 from . import _lib
 from .attention import _DTYPE_CODE
-from .metadata import StepMetadata, sm_count
+from .metadata import StepMetadata, attach, sm_count
 
 BucketOverflow = _lib.BucketOverflow
 
@@ -148,3 +148,81 @@ class DecodeStepGraph:
         _lib.check(_lib.lib().pa_read_device_error(ws, int(clear), ctypes.byref(word),
                                                    torch.cuda.current_stream(self.device).cuda_stream))
         return int(word.value)
+
+
+class ModelDecodeGraph:
+    """One captured all-decode pass of a whole model for a bucket of ``batch`` rows and
+    ``width`` table blocks: the HF forward with this library's paged attention and fused
+    append (the executor's two hooks), then the greedy argmax.  A step only plans its
+    metadata on the host (into a pinned buffer), copies it and the token ids into the
+    graph's static buffers and replays; the per-layer Python and library dispatch of the
+    eager pass is gone.
+
+    Rows past the step's real sequences repeat its last row: the same token at the same
+    position writes the same K/V bytes into the same slot and its output is dropped, so
+    the padding needs no spare pool block.  The plan is padded as in
+    :class:`DecodeStepGraph` (fixed split size, decode-item and combine lists padded with
+    null entries), so every launch parameter inside the graph stays fixed."""
+
+    def __init__(self, executor, batch: int, width: int):
+        ex = executor
+        self.ex, self.B, self.width = ex, int(batch), int(width)
+        dev = ex.device
+        NB, BS, Hkv = ex.num_blocks, ex.block_size, ex.num_kv_heads
+        probe = StepMetadata.plan_host(np.full(self.B, self.width * BS, np.int64), np.ones(self.B, np.int64),
+                                       np.zeros((self.B, self.width), np.int64), num_tokens=self.B,
+                                       pool_num_blocks=NB, block_size=BS, num_kv_heads=Hkv, sm=sm_count(dev))
+        split = int(probe.plan.split_blocks)
+        self.caps = dict(pool_num_blocks=NB, block_size=BS, num_kv_heads=Hkv, split_blocks=split,
+                         width=self.width, items=self.B * (-(-self.width // split)), combine=self.B)
+        shape = StepMetadata.plan_decode_padded(np.ones(self.B, np.int64), np.zeros((self.B, 1), np.int64),
+                                                **self.caps)
+        self.words, self.items = int(shape.plan.words), int(shape.plan.num_decode_items)
+        self._host_t = torch.zeros(self.words, dtype=torch.int32, pin_memory=True)
+        self.meta = StepMetadata(shape.plan, self._host_t.numpy(), NB)
+        self.meta.device_buffer = torch.zeros(self.words, dtype=torch.int32, device=dev)
+        self._ids_host = torch.zeros(1, self.B, dtype=torch.long, pin_memory=True)
+        self.ids = torch.zeros(1, self.B, dtype=torch.long, device=dev)
+        self._copied = torch.cuda.Event()
+        self._copied.record(torch.cuda.current_stream(dev))
+        self.graph = None
+        self.tokens = None
+
+    def set_step(self, context_lens, block_tables, token_ids) -> None:
+        """Plan this step (contexts count the new token) and stage its token ids."""
+        self._copied.synchronize()           # the previous step's copies have left the buffers
+        meta = StepMetadata.plan_decode_padded(context_lens, block_tables, host=self.meta.host, **self.caps)
+        if int(meta.plan.words) != self.words or int(meta.plan.num_decode_items) != self.items:
+            raise RuntimeError("padded plan changed shape inside its bucket")
+        self._ids_host[0].copy_(torch.as_tensor(token_ids, dtype=torch.long))
+
+    def _forward(self):
+        from .executor import StepContext   # the executor module imports this one
+
+        buf, plan = self.meta.device_buffer, self.meta.plan
+        ctx = StepContext(meta=self.meta, block_tables=attach(torch.empty(0, dtype=torch.long, device=buf.device),
+                                                              self.meta),
+                          context_lens=buf[plan.off_context_lens:plan.off_context_lens + self.B],
+                          query_lens=buf[plan.off_query_lens:plan.off_query_lens + self.B], pool=self.ex.pool)
+        logits = self.ex._forward(self.ids, self.meta.q_pos().unsqueeze(0), ctx)
+        return logits[0].argmax(-1)
+
+    def run(self) -> torch.Tensor:
+        """Upload the staged step and run it (capturing it the first time); returns the
+        greedy token of every row (device tensor, valid until the next run)."""
+        dev = self.ex.device
+        stream = torch.cuda.current_stream(dev)
+        self.meta.device_buffer.copy_(self._host_t, non_blocking=True)
+        self.ids.copy_(self._ids_host, non_blocking=True)
+        self._copied.record(stream)
+        if self.graph is None:
+            self.tokens = self._forward()    # eager once: configures every kernel, sizes the workspace
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
+                self.tokens = self._forward()
+            stream.wait_stream(side)
+        self.graph.replay()
+        return self.tokens

@@ -9,7 +9,9 @@ to a temporary copy.  Three arms serve the same requests on the same random-init
 * ``dispatch`` — the same ``PagedExecutor`` with ``ATTENTION=cuda``: only the dispatcher
   changed, so attention runs in this library's kernels;
 * ``executor`` — ``CudaPagedExecutor`` (one-copy step metadata, fused KV append, block
-  moves in one launch) in place of ``PagedExecutor``.
+  moves in one launch) in place of ``PagedExecutor``;
+* ``executor_graphs`` (config 1 mix and recompute preemption) — the same executor with
+  its all-decode passes replayed from captured CUDA graphs of the whole model forward.
 
 The north star's parity target is greedy token ids identical to the gather path for fp32
 GPT-2, which every case asserts for all three arms.  ``PagedEngine`` itself cannot be
@@ -99,7 +101,7 @@ def _make_executor(ref, arm, model, pool, config, cuda_executor, monkeypatch):
         monkeypatch.setattr(config, "attention", "cuda")
         return ref["paged_executor"].PagedExecutor(model, None, pool)
     monkeypatch.setattr(config, "attention", "cuda")
-    return cuda_executor(model, None, pool)
+    return cuda_executor(model, None, pool, decode_graphs=arm == "executor_graphs")
 
 
 def serve(ref, arm, model, requests, *, num_blocks, max_running, config, cuda_executor, monkeypatch, pkg,
@@ -152,7 +154,7 @@ def test_config1_mix_tokens_identical(ref, gpt2, config, cuda_executor, monkeypa
     reference scheduler; 200 requests at concurrency 32 and the first 40 at
     concurrency 4."""
     reqs = config1_requests(n)
-    res = _all_arms(ARMS, ref=ref, model=gpt2, requests=reqs, num_blocks=2048, max_running=concurrency,
+    res = _all_arms(ARMS + ("executor_graphs",), ref=ref, model=gpt2, requests=reqs, num_blocks=2048, max_running=concurrency,
                     config=config, cuda_executor=cuda_executor, monkeypatch=monkeypatch, pkg=pkg)
     _assert_identical(res, reqs)
     assert all(st["preemptions"] == 0 for _, st in res.values())
@@ -187,7 +189,7 @@ def test_preemption_tokens_identical(ref, gpt2, config, cuda_executor, monkeypat
     rng = np.random.default_rng(7)
     reqs = [(rng.integers(0, VOCAB, size=int(rng.integers(60, 161))).tolist(), int(rng.integers(40, 121)))
             for _ in range(10)]
-    arms = ARMS + (("executor_kvpool",) if preemption == "swap" else ())
+    arms = ARMS + (("executor_kvpool",) if preemption == "swap" else ("executor_graphs",))
     res = _all_arms(arms, ref=ref, model=gpt2, requests=reqs, num_blocks=40, max_running=8,
                     config=config, cuda_executor=cuda_executor, monkeypatch=monkeypatch, pkg=pkg)
     _assert_identical(res, reqs)
