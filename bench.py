@@ -1943,6 +1943,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev_d = [events() for _ in range(args.steps)]
         ev_p = [events() for _ in range(args.steps)]
+        alloc0 = _allocator_counts(dev)
         start.record(stream)
         t_host = time.perf_counter()
         host_step_ms = []
@@ -1952,6 +1953,7 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
             host_step_ms.append((time.perf_counter() - t0) * 1e3)
         end.record(stream)
         host_enqueue_ms = (time.perf_counter() - t_host) * 1e3
+        alloc1 = _allocator_counts(dev)
         torch.cuda.synchronize(dev)
         barrier()
         gpu_launches = launches[0]
@@ -2055,6 +2057,10 @@ def run_cuda(args, rank: int, world: int, local_rank: int) -> None:
     # pre-timing synchronize (empty launch queue, so no blocking: the host's own cost)
     spread["host_enqueue_ms"] = round(host_enqueue_ms, 2)
     spread["host_first_step_ms"] = round(host_step_ms[0], 2)
+    spread["host_slowest_step_ms"] = [int(np.argmax(host_step_ms)), round(max(host_step_ms), 2)]
+    # device allocations and allocator retries (free-and-retry after a failed cudaMalloc,
+    # which synchronises the device) inside the timed loop: both should be 0
+    spread["allocator_in_timed_loop"] = {k: alloc1[k] - alloc0[k] for k in alloc0}
 
     source = "MEASURED_PEAKS.json" if peak_kind == "measured" else "fallback"
     line = {
@@ -2095,15 +2101,24 @@ def _prefill_tile(pkg, args, Hq: int, Hkv: int, D: int) -> int:
     return pkg.metadata.prefill_tile_tokens(Hq, Hkv, D)
 
 
+def _allocator_counts(dev) -> dict:
+    """Cumulative counters of torch's caching allocator on `dev`: segments obtained from
+    cudaMalloc and free-and-retry passes."""
+    st = torch.cuda.memory_stats(dev)
+    return {"device_allocs": int(st.get("num_device_alloc", 0)), "alloc_retries": int(st.get("num_alloc_retries", 0))}
+
+
 def _reserve_for_timing(pkg, dev, metas, heads: int, head_dim: int, dtype, max_tokens: int) -> None:
-    """Size the library's workspace for the largest plan and leave a cached block for the
-    largest attention output before any timed region, so no allocation (a cudaMalloc,
+    """Size the library's workspace for the largest plan and leave cached blocks for the
+    largest attention outputs before any timed region, so no allocation (a cudaMalloc,
     or the caching allocator freeing and retrying when HBM is nearly full) happens while
-    launches are being timed."""
+    launches are being timed.  A layer's output is allocated while the previous layer's
+    is still referenced, so up to three of the largest size can be live at once (the
+    timed loop's allocator counters confirm none is made there)."""
     lib = pkg._lib.lib()
     ws = max(int(lib.pa_workspace_bytes(pkg._lib.ctypes.byref(m.plan), heads, head_dim)) for m in metas)
     pkg.attention._workspace(dev, ws)
-    tmp = torch.empty(max_tokens * heads * head_dim, dtype=dtype, device=dev)
+    tmp = [torch.empty(max_tokens * heads * head_dim, dtype=dtype, device=dev) for _ in range(3)]
     del tmp
 
 

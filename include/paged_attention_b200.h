@@ -95,6 +95,7 @@ const char* pa_last_error(void);
 #define PA_LAUNCH_PREFILL_TC 8      /* tcgen05 varlen prefill */
 #define PA_LAUNCH_GENERIC 16        /* generic ragged kernel */
 #define PA_LAUNCH_PREFILL_PAIR 32   /* tcgen05 varlen prefill on CTA pairs (head_dim 128) */
+#define PA_LAUNCH_PREFILL_PERSIST 64 /* persistent tcgen05 varlen prefill (P in TMEM, Q by TMA) */
 int32_t pa_last_launches(void);
 
 /*
@@ -150,7 +151,8 @@ int32_t pa_plan_decode_padded(const int64_t* context_lens, int32_t num_seqs, con
                               pa_step_plan* plan);
 
 /* (token, query-head) rows of one tensor-core prefill tile at this head_dim (128: the
- * single-CTA tcgen05 kernel): plan prefill steps with prefill_tile_tokens =
+ * persistent tcgen05 kernel, or the single-CTA one when the environment variable
+ * PA_PREFILL_KERNEL is "per_tile"): plan prefill steps with prefill_tile_tokens =
  * pa_prefill_tile_rows(head_dim) / (num_heads / num_kv_heads) so their rows take it.  At
  * head_dim 128 a plan tiled at 256 rows runs on the CTA-pair tcgen05 kernel instead (half
  * the K/V bytes per SM; measured slower on B200, so not the default).  No reference

@@ -35,6 +35,7 @@ PA_LAUNCH_COMBINE = 4
 PA_LAUNCH_PREFILL_TC = 8
 PA_LAUNCH_GENERIC = 16
 PA_LAUNCH_PREFILL_PAIR = 32
+PA_LAUNCH_PREFILL_PERSIST = 64
 
 ABI_VERSION = 7
 
@@ -150,7 +151,7 @@ def last_launches() -> set[str]:
     mask = lib().pa_last_launches()
     names = {PA_LAUNCH_DECODE_MMA: "decode_mma", PA_LAUNCH_DECODE_SIMT: "decode_simt",
              PA_LAUNCH_COMBINE: "combine", PA_LAUNCH_PREFILL_TC: "prefill_tc", PA_LAUNCH_GENERIC: "generic",
-             PA_LAUNCH_PREFILL_PAIR: "prefill_pair"}
+             PA_LAUNCH_PREFILL_PAIR: "prefill_pair", PA_LAUNCH_PREFILL_PERSIST: "prefill_persist"}
     return {n for bit, n in names.items() if mask & bit}
 
 

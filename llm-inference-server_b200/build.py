@@ -25,7 +25,7 @@ BUILD = PKG / "_build"
 LIB_NAME = "libpaged_attn_b200.so"
 LIB = PKG / LIB_NAME
 
-CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "prefill_tc.cu", "prefill_pair.cu", "attention_generic.cu", "kv_append.cu",
+CU_SOURCES = ["api.cu", "decode_splitk.cu", "decode_mma.cu", "prefill_tc.cu", "prefill_persist.cu", "prefill_pair.cu", "attention_generic.cu", "kv_append.cu",
               "attention_noalloc.cu",
               "block_copy.cu", "peer_allreduce.cu", "oproj_allreduce.cu"]
 CXX_SOURCES = ["step_plan.cpp"]

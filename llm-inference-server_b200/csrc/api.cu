@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -110,6 +111,34 @@ static int32_t pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int
   cache.emplace(key, map);
   *out = map;
   return PA_OK;
+}
+
+// The query as a 3-D TMA map (head_dim, num_heads, num_tokens) with a box of 64 elements x
+// `group` heads x `rows / group` tokens, 128-byte swizzle: one box is the 128 (token, head)
+// rows of a prefill tile for one 64-column half.
+static int32_t query_tensor_map(const void* query, int32_t num_tokens, int32_t num_heads, int32_t head_dim,
+                                int64_t q_stride_token, int64_t q_stride_head, int dtype, int group, int rows,
+                                CUtensorMap* out) {
+  auto fn = encode_fn();
+  if (!fn) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  const int es = elem_size(dtype);
+  cuuint64_t gdim[3] = {cuuint64_t(head_dim), cuuint64_t(num_heads), cuuint64_t(num_tokens)};
+  cuuint64_t gstride[2] = {cuuint64_t(q_stride_head) * es, cuuint64_t(q_stride_token) * es};
+  cuuint32_t box[3] = {64u, cuuint32_t(group), cuuint32_t(rows / group)};
+  cuuint32_t estride[3] = {1u, 1u, 1u};
+  CUresult r = fn(out, tma_dtype(dtype), 3, const_cast<void*>(query), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled (query) failed (CUresult %d)", int(r));
+  return PA_OK;
+}
+
+// Which kernel serves 128-row prefill tiles: the persistent kernel unless
+// PA_PREFILL_KERNEL is "per_tile" (one CTA per tile).  Read on every call, so one process
+// can run both.
+static bool prefill_persistent_selected() {
+  const char* v = getenv("PA_PREFILL_KERNEL");
+  return !(v && strcmp(v, "per_tile") == 0);
 }
 
 static thread_local int32_t g_last_launches = 0;
@@ -243,16 +272,19 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
       g_last_launches |= PA_LAUNCH_COMBINE;
     }
   }
-  // Prefill rows go to a tcgen05 kernel when the plan's tiles fit one (256 rows = 256 / G
-  // query tokens: the CTA-pair kernel at head_dim 128; 128 rows: the single-CTA kernel)
-  // and query/out rows are 16-byte aligned.
+  // Prefill rows go to a tcgen05 kernel when the plan's tiles fit one and query/out rows
+  // are 16-byte aligned: 128-row tiles to the persistent kernel (or the single-CTA kernel
+  // under PA_PREFILL_KERNEL=per_tile), 256-row tiles to the CTA-pair kernel (head_dim 128).
   const int es = elem_size(dtype);
   const int tile_rows = plan->prefill_tile_tokens * group;
+  const bool persist_prefill = prefill_persist_supported(dtype, head_dim, group, block_size) &&
+                               tile_rows == prefill_tile_rows() && prefill_persistent_selected();
   const bool pair_prefill = prefill_pair_supported(dtype, head_dim, group, block_size) &&
                             tile_rows == prefill_pair_tile_rows();
-  const bool single_prefill = prefill_tc_supported(dtype, head_dim, group, block_size) &&
+  const bool single_prefill = !persist_prefill && prefill_tc_supported(dtype, head_dim, group, block_size) &&
                               tile_rows == prefill_tile_rows();
-  const bool tc_prefill = plan->num_prefill_tiles > 0 && (pair_prefill || single_prefill) && q_stride_dim == 1 &&
+  const bool tc_prefill = plan->num_prefill_tiles > 0 && (persist_prefill || pair_prefill || single_prefill) &&
+                          q_stride_dim == 1 &&
                           (q_stride_token * es) % 16 == 0 && (q_stride_head * es) % 16 == 0 &&
                           reinterpret_cast<uintptr_t>(query) % 16 == 0 && (out_stride_token * es) % 16 == 0 &&
                           (out_stride_head * es) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
@@ -283,10 +315,21 @@ int32_t pa_paged_attention_fwd(const void* query, int64_t q_stride_token, int64_
     f.pool_blocks = int32_t(pool_num_blocks);
     f.qscale = qscale;
     f.err = err;
-    cudaError_t e = pair_prefill ? launch_prefill_pair(dtype, group, tk, tv, f, stream)
-                                 : launch_prefill_tc(dtype, head_dim, group, tk, tv, f, stream);
+    cudaError_t e;
+    if (persist_prefill) {
+      CUtensorMap tq;
+      rc = query_tensor_map(query, num_tokens, num_heads, head_dim, q_stride_token, q_stride_head, dtype, group,
+                            tile_rows, &tq);
+      if (rc != PA_OK) return rc;
+      e = launch_prefill_persist(dtype, head_dim, group, tk, tv, tq, f, stream);
+    } else if (pair_prefill) {
+      e = launch_prefill_pair(dtype, group, tk, tv, f, stream);
+    } else {
+      e = launch_prefill_tc(dtype, head_dim, group, tk, tv, f, stream);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 prefill launch");
-    g_last_launches |= pair_prefill ? PA_LAUNCH_PREFILL_PAIR : PA_LAUNCH_PREFILL_TC;
+    g_last_launches |= persist_prefill ? PA_LAUNCH_PREFILL_PERSIST
+                                       : (pair_prefill ? PA_LAUNCH_PREFILL_PAIR : PA_LAUNCH_PREFILL_TC);
   }
   const bool decode_left = plan->num_decode_seqs > 0 && !fast_decode;
   const bool prefill_left = plan->num_prefill_tokens > 0 && !tc_prefill;
@@ -415,7 +458,7 @@ int32_t pa_scatter_blocks(void* const* k_pools, void* const* v_pools, int32_t nu
 }
 
 int32_t pa_prefill_tile_rows(int32_t head_dim) {
-  (void)head_dim;  // the single-CTA kernel serves every head_dim by default (the pair kernel measured slower)
+  (void)head_dim;  // 128-row tiles serve every head_dim by default (the 256-row pair kernel measured slower)
   return pa::prefill_tile_rows();
 }
 

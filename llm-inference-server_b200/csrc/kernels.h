@@ -171,6 +171,12 @@ bool prefill_pair_supported(int dtype, int head_dim, int group, int block_size);
 int prefill_pair_tile_rows();
 cudaError_t launch_prefill_pair(int dtype, int group, const CUtensorMap& tk, const CUtensorMap& tv,
                                 const PrefillParams& p, cudaStream_t stream);
+// Persistent tcgen05 prefill over the same 128-row tiles: two CTAs per SM, Q by TMA from
+// `tq` (the query as (head_dim, num_heads, num_tokens), box (64, G, 128 / G), 128-byte
+// swizzle), P kept in TMEM.
+bool prefill_persist_supported(int dtype, int head_dim, int group, int block_size);
+cudaError_t launch_prefill_persist(int dtype, int head_dim, int group, const CUtensorMap& tk, const CUtensorMap& tv,
+                                   const CUtensorMap& tq, const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_block_copy(const BlockCopyParams& p, cudaStream_t stream);
 cudaError_t launch_peer_allreduce(int dtype, const PeerReduceParams& p, int grid, cudaStream_t stream);

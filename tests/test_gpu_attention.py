@@ -8,6 +8,8 @@ own kernel tier allows 1e-4, tests/test_paged_attention_triton.py:165-169), fp16
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -22,10 +24,17 @@ NAME = {v: k for k, v in DT.items()}
 DEV = "cuda"
 
 
-def _pf(d: int) -> str:
-    """The tcgen05 prefill kernel a default plan runs at this head_dim (the single-CTA
-    kernel; the CTA-pair kernel runs for plans tiled at 256 rows)."""
-    return "prefill_tc"
+def _pf(rows: int = 128) -> str:
+    """The tcgen05 prefill kernel a plan tiled at `rows` runs: 128-row tiles the persistent
+    kernel (the single-CTA kernel under PA_PREFILL_KERNEL=per_tile), 256-row tiles the
+    CTA-pair kernel."""
+    if rows == 256:
+        return "prefill_pair"
+    return "prefill_tc" if os.environ.get("PA_PREFILL_KERNEL") == "per_tile" else "prefill_persist"
+
+
+# (PA_PREFILL_KERNEL value, tile rows) of every tcgen05 prefill kernel
+PREFILL_KERNELS = [("persistent", 128), ("per_tile", 128), ("per_tile", 256)]
 
 
 def _close(got: np.ndarray, ref: np.ndarray, dt: str, what: str = ""):
@@ -251,7 +260,7 @@ def test_tensor_core_prefill_churn_shape(pkg, oracle):
     lengths = [(int(n), int(n)) for n in rng.integers(256, 2049, size=3)]
     q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=32, kv_heads=8, dtype=torch.bfloat16, seed=3)
     out = _run(pkg, q, kp, vp, bt, cl, ql, 128 ** -0.5).float().cpu().numpy()
-    assert pkg._lib.last_launches() == {"prefill_tc"}
+    assert pkg._lib.last_launches() == {_pf()}
     pick = [int(np.argmin([c for c, _ in lengths]))]
     sub = compact_subbatch(q, kp, vp, bt, cl, ql, lengths, pick, 16)
     ref = oracle.paged_attention_gather(*sub, 128 ** -0.5, "bf16")
@@ -282,7 +291,7 @@ def test_shared_prefix_blocks_match_oracle(pkg, oracle):
     cl = torch.tensor(ctx, dtype=torch.long)
     ql = torch.tensor(suffixes, dtype=torch.long)
     out = _run(pkg, q, kp, vp, tables, cl, ql, d ** -0.5).float().cpu().numpy()
-    assert {"prefill_tc", "decode_mma"} <= pkg._lib.last_launches()
+    assert {_pf(), "decode_mma"} <= pkg._lib.last_launches()
     ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), tables.numpy(),
                                         cl.numpy(), ql.numpy(), d ** -0.5, "bf16")
     _close(out, ref, "bf16", "shared prefix blocks")
@@ -299,11 +308,11 @@ def _with_tiles(pkg, bt, cl, ql, num_tokens, nb, kv_heads, tile_tokens):
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 @pytest.mark.parametrize("heads,kv_heads", [(16, 16), (16, 8), (32, 8), (64, 8)])
-def test_pair_prefill_matches_single_cta_kernel_and_oracle(pkg, oracle, dtype, heads, kv_heads):
-    """The CTA-pair prefill (256-row tiles over two SMs, each CTA holding half of every K/V
-    tile) against the single-CTA tcgen05 kernel on the same batch and the oracle, for GQA
-    groups 1/2/4/8 at head_dim 128: tiles whose second CTA has few or no tokens, prompts
-    shorter than one pair, prefix hits, contexts ending mid-block and mid-KV-tile."""
+def test_prefill_kernels_agree_with_each_other_and_oracle(pkg, oracle, monkeypatch, dtype, heads, kv_heads):
+    """Every tcgen05 prefill kernel (persistent, single-CTA, CTA pair)
+    on the same batch against the oracle and each other, for GQA groups 1/2/4/8 at
+    head_dim 128: tiles whose second half has few or no tokens, prompts shorter than one
+    tile, prefix hits, contexts ending mid-block and mid-KV-tile."""
     g = heads // kv_heads
     lengths = PREFILL_LENGTHS + [(256 // g + 1, 256 // g + 1), (128 // g, 128 // g), (128 // g + 3, 128 // g + 3),
                                  (1000, 256 // g), (333, 128 // g - 1)]
@@ -311,25 +320,27 @@ def test_pair_prefill_matches_single_cta_kernel_and_oracle(pkg, oracle, dtype, h
                                          seed=21)
     qd, kd, vd = q.to(DEV), kp.to(DEV), vp.to(DEV)
     cld, qld = cl.to(DEV), ql.to(DEV)
-    pair_bt = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, 256 // g)
-    pair = pkg.paged_attention_cuda(qd, kd, vd, pair_bt, cld, qld, 128 ** -0.5).float().cpu().numpy()
-    assert "prefill_pair" in pkg._lib.last_launches() and "prefill_tc" not in pkg._lib.last_launches()
-    single_bt = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, 128 // g)
-    single = pkg.paged_attention_cuda(qd, kd, vd, single_bt, cld, qld, 128 ** -0.5).float().cpu().numpy()
-    assert "prefill_tc" in pkg._lib.last_launches() and "prefill_pair" not in pkg._lib.last_launches()
     ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
                                         cl.numpy(), ql.numpy(), 128 ** -0.5, dtype)
-    _close(pair, ref, dtype, "CTA-pair prefill")
-    _close(single, ref, dtype, "single-CTA prefill")
-    np.testing.assert_allclose(pair, single, atol=1e-2, rtol=1e-2)
+    outs = {}
+    for kernel, rows in PREFILL_KERNELS:
+        monkeypatch.setenv("PA_PREFILL_KERNEL", kernel)
+        btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, rows // g)
+        out = pkg.paged_attention_cuda(qd, kd, vd, btd, cld, qld, 128 ** -0.5).float().cpu().numpy()
+        assert _pf(rows) in pkg._lib.last_launches(), (kernel, rows, pkg._lib.last_launches())
+        _close(out, ref, dtype, f"{kernel} prefill, {rows}-row tiles")
+        outs[(kernel, rows)] = out
+    for key, out in outs.items():
+        np.testing.assert_allclose(out, outs[("per_tile", 128)], atol=1e-2, rtol=1e-2, err_msg=str(key))
     assert pkg.read_device_error() == 0
 
 
-@pytest.mark.parametrize("tiles", ["pair", "single"])
-def test_prefill_ignores_stale_rows_past_the_context(pkg, oracle, tiles):
+@pytest.mark.parametrize("kernel,rows", PREFILL_KERNELS)
+def test_prefill_ignores_stale_rows_past_the_context(pkg, oracle, monkeypatch, kernel, rows):
     """The reference slices every sequence's keys to its context (attention.py:171-172),
     so whatever a freed-and-reused block holds past the context never reaches it.  Fill
     those rows of K and V with NaN: the tcgen05 kernels must give the oracle's result."""
+    monkeypatch.setenv("PA_PREFILL_KERNEL", kernel)
     lengths = [(70, 70), (100, 37), (17, 17), (1000, 999), (130, 130)]
     heads, kv_heads = 32, 8
     q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=128, heads=heads, kv_heads=kv_heads,
@@ -339,15 +350,34 @@ def test_prefill_ignores_stale_rows_past_the_context(pkg, oracle, tiles):
         last = int(bt[i, (c - 1) // 16])
         kp_bad[last, c % 16 or 16:] = float("nan")
         vp_bad[last, c % 16 or 16:] = float("nan")
-    tile = (256 if tiles == "pair" else 128) // (heads // kv_heads)
-    btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, tile)
+    btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, rows // (heads // kv_heads))
     out = pkg.paged_attention_cuda(q.to(DEV), kp_bad.to(DEV), vp_bad.to(DEV), btd, cl.to(DEV), ql.to(DEV),
                                    128 ** -0.5).float().cpu().numpy()
-    assert ("prefill_pair" if tiles == "pair" else "prefill_tc") in pkg._lib.last_launches()
+    assert _pf(rows) in pkg._lib.last_launches()
     assert np.isfinite(out).all()
     ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
                                         cl.numpy(), ql.numpy(), 128 ** -0.5, "bf16")
-    _close(out, ref, "bf16", f"{tiles} prefill with NaN past the context")
+    _close(out, ref, "bf16", f"{kernel} prefill ({rows} rows) with NaN past the context")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("kernel,rows", [("persistent", 128), ("per_tile", 128)])
+def test_prefill_head_dim_64_kernels(pkg, oracle, monkeypatch, dtype, kernel, rows):
+    """head_dim 64 (one 64-column half per row) on the tcgen05 prefill kernels that serve
+    it, GQA group 4, with ragged prompts, prefix hits and a decode row in the batch."""
+    monkeypatch.setenv("PA_PREFILL_KERNEL", kernel)
+    heads, kv_heads = 16, 4
+    lengths = [(300, 300), (77, 77), (513, 129), (64, 64), (1000, 1), (200, 33)]
+    q, kp, vp, bt, cl, ql = ragged_batch(lengths, bs=16, d=64, heads=heads, kv_heads=kv_heads, dtype=DT[dtype],
+                                         seed=31)
+    btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, rows // (heads // kv_heads))
+    out = pkg.paged_attention_cuda(q.to(DEV), kp.to(DEV), vp.to(DEV), btd, cl.to(DEV), ql.to(DEV),
+                                   64 ** -0.5).float().cpu().numpy()
+    assert _pf(rows) in pkg._lib.last_launches()
+    ref = oracle.paged_attention_gather(q.float().numpy(), kp.float().numpy(), vp.float().numpy(), bt.numpy(),
+                                        cl.numpy(), ql.numpy(), 64 ** -0.5, dtype)
+    _close(out, ref, dtype, f"{kernel} prefill, head_dim 64, {rows}-row tiles")
+    assert pkg.read_device_error() == 0
 
 
 def _torch_gather_reference(q, kp, vp, bt, cl, ql, scale, rows=512):
@@ -408,7 +438,7 @@ def test_full_size_batches_every_sequence(pkg, oracle, workload):
     q, kp, vp, bt, cl, ql = batch
     out = pkg.paged_attention_cuda(q, kp, vp, bt.to(DEV), cl.to(DEV), ql.to(DEV), d ** -0.5)
     if workload == "config3-churn":
-        assert pkg._lib.last_launches() == {"prefill_tc"}
+        assert pkg._lib.last_launches() == {_pf()}
     ref = _torch_gather_reference(q, kp, vp, bt, cl, ql, d ** -0.5).cpu().numpy()
     _close(out.float().cpu().numpy(), ref, dt, workload)
     # the torch restatement itself, pinned to the oracle on the shortest and longest rows
@@ -419,7 +449,7 @@ def test_full_size_batches_every_sequence(pkg, oracle, workload):
     assert pkg.read_device_error() == 0
 
 
-def test_long_context_prefill_matches_reference(pkg, oracle):
+def test_long_context_prefill_matches_reference(pkg, oracle, monkeypatch):
     """Long rows of the tcgen05 prefill at the Llama-8B shape: a 4,600-token prompt and a
     prefix-cache hit of 700 new tokens over a 9,300-token context (plus a decode row),
     every row compared with the gather arithmetic in torch float32.  That torch reference
@@ -437,9 +467,10 @@ def test_long_context_prefill_matches_reference(pkg, oracle):
     q, kp, vp, bt, cl, ql = ragged_batch_device(lengths, bs=16, d=d, heads=heads, kv_heads=kv_heads,
                                                 dtype=torch.bfloat16, device=DEV, seed=6)
     ref = _torch_gather_reference(q, kp, vp, bt, cl, ql, d ** -0.5).cpu().numpy()
-    for rows, kernel in ((128, "prefill_tc"), (256, "prefill_pair")):
+    for kernel, rows in PREFILL_KERNELS:
+        monkeypatch.setenv("PA_PREFILL_KERNEL", kernel)
         btd = _with_tiles(pkg, bt, cl, ql, q.shape[0], kp.shape[0], kv_heads, rows // (heads // kv_heads))
         out = pkg.paged_attention_cuda(q, kp, vp, btd, cl.to(DEV), ql.to(DEV), d ** -0.5)
-        assert {kernel, "decode_mma"} <= pkg._lib.last_launches()
-        _close(out.float().cpu().numpy(), ref, "bf16", f"long-context prefill ({kernel})")
+        assert {_pf(rows), "decode_mma"} <= pkg._lib.last_launches()
+        _close(out.float().cpu().numpy(), ref, "bf16", f"long-context prefill ({kernel}, {rows} rows)")
     assert pkg.read_device_error() == 0

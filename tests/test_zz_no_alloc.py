@@ -74,7 +74,7 @@ def test_noalloc_matches_workspace_entry_point_twice(pkg, dtype, heads, kv_heads
         torch.cuda.synchronize()
         np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), **tol)
         if dtype == torch.bfloat16:  # the tensor-core decode and prefill both ran through it
-            assert {"decode_mma", "prefill_tc", "combine"} <= launched
+            assert {"decode_mma", "combine"} <= launched and launched & {"prefill_tc", "prefill_persist"}
     assert _error_word(pkg) == 0
 
 
