@@ -30,6 +30,9 @@
 // rare O rescale, the epilogue; warp 4: producer of item metadata (a 2-slot descriptor
 // ring), Q and K (3-stage ring); warp 5: TMEM allocation and MMA issue, S = Q.K^T (SS,
 // M=128, N=64) and O += P.V (TS, M=128, N=head_dim); warp 6: producer of V (2-stage ring).
+// The MMA warp's issue rate bounds the kernel, so it commits twice per tile: "S retired"
+// (one barrier per K stage, also freeing that stage) and "P.V retired" (one per P buffer,
+// also freeing the V stage of the same index).
 // TMEM columns: S [0, 64), O [64, 64 + D), P buffers [64 + D, 128 + D).
 //
 // Every mbarrier wait is bounded; the TMEM allocation is released on every path.
@@ -44,7 +47,7 @@ constexpr int kPpRows = 128;
 constexpr int kPpKeys = 64;
 constexpr int kPpBlocks = kPpKeys / 16;
 constexpr int kPpKStages = 3;
-constexpr int kPpVStages = 2;
+constexpr int kPpVStages = 2;  // equal to the P buffer count: one "P.V retired" barrier frees both
 constexpr int kPpThreads = 224;
 constexpr int kPpQHalf = kPpRows * 128;   // 128 rows x 64 elements, 128-byte swizzle
 constexpr int kPpKvHalf = kPpKeys * 128;  // 64 keys x 64 elements
@@ -72,10 +75,14 @@ struct PpItem {  // one work item, written by the producer, read by the other ro
 };
 
 struct PpBars {
-  uint64_t k_full[kPpKStages], k_empty[kPpKStages];
-  uint64_t v_full[kPpVStages], v_empty[kPpVStages];
-  uint64_t q_full, q_empty, s_full, s_consumed;
-  uint64_t p_full[2], p_free[2];  // P buffer written / the P.V that read it retired
+  // S of tile g retired: s_full[g % kPpKStages], waited on by the softmax (the scores are
+  // ready) and by the K producer (K stage g % kPpKStages is free again).
+  uint64_t k_full[kPpKStages], s_full[kPpKStages];
+  uint64_t v_full[kPpVStages];
+  uint64_t q_full, q_empty, s_consumed;
+  // P buffer written / the P.V that read it retired.  V stages and P buffers are both
+  // indexed by tile % 2, so p_free[s] also frees V stage s for the V producer.
+  uint64_t p_full[2], p_free[2];
   uint64_t d_full[2], d_empty[2];
   uint32_t tmem_base;
 };
@@ -113,15 +120,13 @@ __global__ void __launch_bounds__(kPpThreads, 2)
   if (tid == 0) {
     for (int s = 0; s < kPpKStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
-      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->s_full[s], 1);
     }
     for (int s = 0; s < kPpVStages; ++s) {
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
-    mbar_init(&bars->s_full, 1);
     mbar_init(&bars->s_consumed, 128);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->p_full[s], 128);
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
           phys = 0;
         }
         if (g >= kPpKStages)
-          pok = __all_sync(0xffffffffu, mbar_wait(&bars->k_empty[s], ((g / kPpKStages) - 1) & 1));
+          pok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[s], ((g / kPpKStages) - 1) & 1));
         if (!pok) break;
         if (lane == 0) mbar_arrive_expect_tx(&bars->k_full[s], uint32_t(nload * NH * 2048));
         __syncwarp();
@@ -242,7 +247,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
         int phys = __shfl_sync(0xffffffffu, ids_cur, (j & 7) * kPpBlocks + (my_b & (kPpBlocks - 1)));
         if (mine && (phys < 0 || phys >= p.pool_blocks)) phys = 0;  // reported by the K producer
         if (g >= kPpVStages)
-          pok = __all_sync(0xffffffffu, mbar_wait(&bars->v_empty[s], ((g / kPpVStages) - 1) & 1));
+          pok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[s], ((g / kPpVStages) - 1) & 1));
         if (!pok) break;
         if (lane == 0) mbar_arrive_expect_tx(&bars->v_full[s], uint32_t(nload * NH * 2048));
         __syncwarp();
@@ -279,8 +284,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
             const uint64_t bd = smem_desc_sw128(v0 + kk * 2048, kPpKvHalf, 1024);
             umma_f16_ts(tO, tP + pb * (kPpKeys / 2) + 8 * kk, bd, idO, (!first || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&bars->p_free[pb]);
-          umma_commit(&bars->v_empty[vs]);
+          umma_commit(&bars->p_free[pb]);  // also frees V stage vs (== pb)
           return true;
         };
         if (!mbar_wait(&bars->q_full, k & 1)) ok = false;
@@ -299,8 +303,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
             const uint64_t bd = smem_desc_sw128(k0 + (kk >> 2) * kPpKvHalf + (kk & 3) * 32, 16, 1024);
             umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&bars->s_full);
-          umma_commit(&bars->k_empty[s]);
+          umma_commit(&bars->s_full[s]);  // scores ready, K stage s free
           if (j == nkv - 1) umma_commit(&bars->q_empty);
           if (j > 0 && !issue_pv(g - 1, j == 1)) ok = false;
         }
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
 
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < d.nkv; ++j, ++g) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full, g & 1));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[g % kPpKStages], (g / kPpKStages) & 1));
         if (!ok) break;
         tc_fence_after();
         uint32_t sr[kPpKeys];
