@@ -26,13 +26,14 @@
 //     A operand from tensor memory: no shared-memory P, no proxy fence per tile, and the
 //     softmax waits on P.V only to reuse a P buffer two tiles later or to rescale O.
 //
-// Roles (224 threads): warps 0-3 softmax, one thread per row (TMEM lane r): the scores, the
+// Roles (256 threads): warps 0-3 softmax, one thread per row (TMEM lane r): the scores, the
 // rare O rescale, the epilogue; warp 4: producer of item metadata (a 2-slot descriptor
-// ring), Q and K (3-stage ring); warp 5: TMEM allocation and MMA issue, S = Q.K^T (SS,
-// M=128, N=64) and O += P.V (TS, M=128, N=head_dim); warp 6: producer of V (2-stage ring).
-// The MMA warp's issue rate bounds the kernel, so it commits twice per tile: "S retired"
-// (one barrier per K stage, also freeing that stage) and "P.V retired" (one per P buffer,
-// also freeing the V stage of the same index).
+// ring), Q and K (3-stage ring); warp 5: TMEM allocation and the S = Q.K^T issue (SS,
+// M=128, N=64); warp 6: producer of V (2-stage ring); warp 7: the O += P.V issue (TS,
+// M=128, N=head_dim).  MMA issue bounds the kernel, so S and P.V go out from two threads
+// (neither waits behind the other's dependencies) with two commits per tile between them:
+// "S retired" (one barrier per K stage, also freeing that stage) and "P.V retired" (one
+// per P buffer, also freeing the V stage of the same index).
 // TMEM columns: S [0, 64), O [64, 64 + D), P buffers [64 + D, 128 + D).
 //
 // Every mbarrier wait is bounded; the TMEM allocation is released on every path.
@@ -48,10 +49,10 @@ constexpr int kPpKeys = 64;
 constexpr int kPpBlocks = kPpKeys / 16;
 constexpr int kPpKStages = 3;
 constexpr int kPpVStages = 2;  // equal to the P buffer count: one "P.V retired" barrier frees both
-constexpr int kPpThreads = 224;
+constexpr int kPpThreads = 256;
 constexpr int kPpQHalf = kPpRows * 128;   // 128 rows x 64 elements, 128-byte swizzle
 constexpr int kPpKvHalf = kPpKeys * 128;  // 64 keys x 64 elements
-constexpr int kPpDescConsumers = 6;       // 4 softmax warps, MMA warp, V producer
+constexpr int kPpDescConsumers = 7;       // 4 softmax warps, S and P.V issuers, V producer
 constexpr float kPpLazyRescale = 8.f;
 
 template <int D>
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
     }
     if (!pok && lane == 0) set_error(p.err, kErrWaitTimeout);
   } else if (warp == 5) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ S issuer
     bool ok = true;
     int g = 0;  // tiles issued so far (all items)
     for (int k = 0; ok && pp_item(k, b, grid, items) >= 0; ++k) {
@@ -270,23 +271,7 @@ __global__ void __launch_bounds__(kPpThreads, 2)
       if (lane == 0) {
         mbar_arrive(&bars->d_empty[slot]);
         constexpr uint32_t idS = idesc_f16<T>(kPpRows, kPpKeys, false);
-        constexpr uint32_t idO = idesc_f16<T>(kPpRows, D, true);
         const uint32_t q0 = smem_u32(sQ);
-        // O += P_h.V_h, the item's first P.V overwriting O.
-        auto issue_pv = [&](int h, bool first) -> bool {
-          const int pb = h & 1, vs = h % kPpVStages;
-          if (!mbar_wait(&bars->p_full[pb], (h >> 1) & 1) || !mbar_wait(&bars->v_full[vs], (h / kPpVStages) & 1))
-            return false;
-          tc_fence_after();
-          const uint32_t v0 = smem_u32(sV + vs * C::KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < kPpKeys / 16; ++kk) {
-            const uint64_t bd = smem_desc_sw128(v0 + kk * 2048, kPpKvHalf, 1024);
-            umma_f16_ts(tO, tP + pb * (kPpKeys / 2) + 8 * kk, bd, idO, (!first || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&bars->p_free[pb]);  // also frees V stage vs (== pb)
-          return true;
-        };
         if (!mbar_wait(&bars->q_full, k & 1)) ok = false;
         for (int j = 0; j < nkv && ok; ++j, ++g) {
           const int s = g % kPpKStages;
@@ -305,9 +290,43 @@ __global__ void __launch_bounds__(kPpThreads, 2)
           }
           umma_commit(&bars->s_full[s]);  // scores ready, K stage s free
           if (j == nkv - 1) umma_commit(&bars->q_empty);
-          if (j > 0 && !issue_pv(g - 1, j == 1)) ok = false;
         }
-        if (ok && !issue_pv(g - 1, nkv == 1)) ok = false;
+        if (!ok) set_error(p.err, kErrWaitTimeout);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      g = __shfl_sync(0xffffffffu, g, 0);
+    }
+  } else if (warp == 7) {
+    // ------------------------------------------------------------ P.V issuer
+    // O += P_h.V_h once the softmax has written P_h (after any rescale of O and, for the
+    // item's first tile, after the previous item's epilogue read O) and V_h has landed;
+    // the item's first P.V overwrites O.  S and P.V touch disjoint TMEM columns.
+    bool ok = true;
+    int g = 0;
+    for (int k = 0; ok && pp_item(k, b, grid, items) >= 0; ++k) {
+      const int slot = k & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[slot], (k >> 1) & 1));
+      if (!ok) break;
+      const int nkv = desc[slot].nkv;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars->d_empty[slot]);
+        constexpr uint32_t idO = idesc_f16<T>(kPpRows, D, true);
+        for (int j = 0; j < nkv && ok; ++j, ++g) {
+          const int pb = g & 1, vs = g % kPpVStages;
+          if (!mbar_wait(&bars->p_full[pb], (g >> 1) & 1) || !mbar_wait(&bars->v_full[vs], (g / kPpVStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t v0 = smem_u32(sV + vs * C::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kPpKeys / 16; ++kk) {
+            const uint64_t bd = smem_desc_sw128(v0 + kk * 2048, kPpKvHalf, 1024);
+            umma_f16_ts(tO, tP + pb * (kPpKeys / 2) + 8 * kk, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars->p_free[pb]);  // also frees V stage vs (== pb)
+        }
         if (!ok) set_error(p.err, kErrWaitTimeout);
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
