@@ -29,6 +29,28 @@ def test_library_exports_every_declared_symbol(pkg):
         assert f" T {name}" in dyn, f"{name} is not a dynamic export"
 
 
+def test_launch_bits_match_the_header(pkg, monkeypatch):
+    """Every PA_LAUNCH_* bit the header defines has the same value in the Python binding and
+    a name in last_launches(), and the bits are distinct, so the tests that check which
+    kernel served a call read the library's own report."""
+    import re
+
+    text = pkg._lib.HEADER.read_text()
+    bits = {m.group(1): int(m.group(2)) for m in re.finditer(r"^#define (PA_LAUNCH_\w+) (\d+)", text, flags=re.M)}
+    assert len(bits) >= 7
+    assert len(set(bits.values())) == len(bits) and all(v & (v - 1) == 0 for v in bits.values())
+    for name, value in bits.items():
+        assert getattr(pkg._lib, name) == value, name
+
+    class _Lib:  # last_launches() reads the mask from the library; feed it every bit at once
+        @staticmethod
+        def pa_last_launches():
+            return sum(bits.values())
+
+    monkeypatch.setattr(pkg._lib, "lib", lambda: _Lib())
+    assert len(pkg._lib.last_launches()) == len(bits)
+
+
 def test_every_entry_point_cites_its_reference_interface_or_has_none(pkg):
     """Each declaration's doc block (the nearest comment opening at column 0 before it)
     names the reference interface it replaces (inference_server/...:line) or says it has
